@@ -1,0 +1,150 @@
+/*
+ * wfattn.h -- C ABI of libwfattn, the B200 (sm_100a) attention library that
+ * replaces the WarpForth attention kernel (demo/attention.forth compiled to
+ * demo/attention.ptx in tetsuo-cpp/warpforth) and its launch paths.
+ *
+ * Conventions shared by every entry point:
+ *  - All tensor pointers are DEVICE pointers owned by the caller.  The library
+ *    never allocates device memory on these paths; outputs are fully
+ *    overwritten over their logical extent.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream,
+ *    which is what the reference launches on: warpforth-runner.cpp:318-319).
+ *    Every call is asynchronous with respect to the host, like the reference's
+ *    cuLaunchKernel.
+ *  - Errors come back as a wfattn_status_t; nothing calls exit().  The text of
+ *    the last failure on the calling thread is available from
+ *    wfattn_last_error().  Argument checks happen on the host before any
+ *    launch.
+ *  - Strides are in ELEMENTS, ordered {batch, head, seq}; the head_dim stride
+ *    must be 1.  A NULL stride pointer means the contiguous [B, H, S, D] layout.
+ *  - Causal masking aligns the query block with the END of the key block:
+ *    query i (0-based) sees keys t <= i + (seq_k - seq_q).  With
+ *    seq_q == seq_k this is exactly the reference's `t > row` mask
+ *    (demo/attention.forth:31-33).  Causal calls require seq_k >= seq_q.
+ *  - The library is thread-safe: the only global state is a per-device
+ *    status word and a per-device cache of properties, set up under a mutex.
+ */
+#ifndef WFATTN_H
+#define WFATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WFATTN_API __attribute__((visibility("default")))
+#else
+#define WFATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  WFATTN_OK = 0,
+  WFATTN_INVALID_ARG = 1,  /* bad pointer, size, stride, alignment or geometry */
+  WFATTN_UNSUPPORTED = 2,  /* valid request outside what the kernels implement */
+  WFATTN_CUDA_ERROR = 3,   /* a CUDA runtime/driver call failed */
+  WFATTN_TIMEOUT = 4       /* a bounded device-side wait expired (see wfattn_device_status) */
+} wfattn_status_t;
+
+typedef enum {
+  WFATTN_DTYPE_F32 = 0,  /* f32 I/O; f32 arithmetic held to <= 1e-5 abs of the f64 reference */
+  WFATTN_DTYPE_BF16 = 1  /* bf16 I/O; f32 accumulation on tcgen05 tensor cores */
+} wfattn_dtype_t;
+
+typedef struct {
+  unsigned int x, y, z;
+} wfattn_dim3;
+
+/* Library version as 10000*major + 100*minor + patch. */
+WFATTN_API int wfattn_version(void);
+
+/* Static text for a status code. */
+WFATTN_API const char *wfattn_status_string(wfattn_status_t status);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+WFATTN_API const char *wfattn_last_error(void);
+
+/*
+ * Drop-in for the reference kernel launch.
+ *
+ * Replaces: `attention(Q, K, V, O, SEQ_LEN, HEAD_DIM)` declared at
+ * demo/attention.forth:8-16 (bare-pointer ABI: lib/Conversion/Passes.cpp:42-45),
+ * as launched by tools/warpforth-runner/warpforth-runner.cpp:313-319 and by
+ * demo/warpforth.py:40-49.  Q, K, V, O are contiguous row-major [seq_len,
+ * head_dim] f32 arrays of ONE head; O is overwritten.  The score scale is
+ * 1/sqrt(head_dim) and the mask is causal, as in the reference.
+ *
+ * `grid` and `block` may be NULL.  When given they must be the reference's
+ * geometry (seq_len, 1, 1), otherwise WFATTN_INVALID_ARG; the library then
+ * picks its own launch shape.  Unlike the reference (valid for
+ * 2 <= seq_len <= 1024), any seq_len >= 1 is accepted; head_dim <= 256.
+ */
+WFATTN_API wfattn_status_t wfattn_attention(const float *Q, const float *K, const float *V, float *O,
+                                 int64_t seq_len, int64_t head_dim, const wfattn_dim3 *grid,
+                                 const wfattn_dim3 *block, void *stream);
+
+/*
+ * Batched multi-head scaled-dot-product attention over [B, H, S, D] tensors
+ * (prefill: every query row of every head in one launch).
+ *
+ * Replaces: the per-head launch loop of demo/gpt2_generate.py:42-50 (one
+ * `attention` launch per head, batch index 0 only) with one call over all
+ * batches and heads, reading the strided q/k/v views directly.
+ *
+ * dtype WFATTN_DTYPE_F32: q, k, v, o are f32; any head_dim in [1, 256].
+ * dtype WFATTN_DTYPE_BF16: q, k, v, o are bf16; head_dim must be 64; the
+ *   q/k/v base pointers must be 16-byte aligned and their batch/head/seq
+ *   strides multiples of 8 elements (TMA requirements).
+ * scale <= 0 selects 1/sqrt(head_dim).
+ */
+WFATTN_API wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t seq_q,
+                               int64_t seq_k, int64_t head_dim, const void *q,
+                               const int64_t *q_strides, const void *k, const int64_t *k_strides,
+                               const void *v, const int64_t *v_strides, void *o,
+                               const int64_t *o_strides, float scale, int causal, void *stream);
+
+/*
+ * Decode attention: one query token per (batch, head) against a padded KV
+ * cache, split over key chunks and combined (split-KV).
+ *
+ * Replaces: nothing in the reference, which has no KV cache
+ * (demo/README.md:45, demo/gpt2_generate.py:84 use_cache=False); this is the
+ * decode step the GPT-2 demo would take with a cache.
+ *
+ * q:        bf16 [B, H, D] with strides q_strides = {batch, head} (NULL = contiguous)
+ * k_cache:  bf16 [B, H, max_kv_len, D] with k_strides = {batch, head, seq};
+ *           the seq stride must be D (the rows of one head are contiguous)
+ * v_cache:  bf16, same shape and rule, v_strides
+ * kv_lens:  DEVICE int32 [B], 1 <= kv_lens[b] <= max_kv_len (keys past
+ *           kv_lens[b] are never read)
+ * o:        f32 [B, H, D] with o_strides = {batch, head} (NULL = contiguous)
+ * head_dim must be 64.  scale <= 0 selects 1/sqrt(head_dim).
+ * workspace: device scratch of at least wfattn_decode_workspace_size() bytes,
+ *           16-byte aligned, owned by the caller; calls that share a
+ *           workspace must be ordered on one stream.
+ */
+WFATTN_API size_t wfattn_decode_workspace_size(int64_t batch, int64_t heads, int64_t max_kv_len,
+                                    int64_t head_dim);
+
+WFATTN_API wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, int64_t max_kv_len,
+                              const void *q, const int64_t *q_strides, const void *k_cache,
+                              const int64_t *k_strides, const void *v_cache,
+                              const int64_t *v_strides, const int32_t *kv_lens, float *o,
+                              const int64_t *o_strides, float scale, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
+/*
+ * Reads (and optionally clears) the device-side status word of the current
+ * device: WFATTN_OK, or WFATTN_TIMEOUT when a bounded wait inside a kernel
+ * (TMA/MMA pipeline barrier) gave up and the kernel returned early.
+ * Synchronizes `stream` first.
+ */
+WFATTN_API wfattn_status_t wfattn_device_status(void *stream, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WFATTN_H */

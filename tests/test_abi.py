@@ -1,0 +1,89 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol that
+include/wfattn.h declares, and rejects bad arguments on the host before any
+CUDA call (the reference's runner exits on such input instead:
+tools/warpforth-runner/warpforth-runner.cpp:93-199,255-283)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from warpforth_b200 import _lib
+
+
+def _declared_symbols() -> list[str]:
+    text = (ROOT / "include" / "wfattn.h").read_text()
+    return re.findall(r"WFATTN_API\s+[\w\s\*]*?\b(wfattn_\w+)\s*\(", text)
+
+
+def test_header_declares_the_bound_symbols():
+    assert sorted(_declared_symbols()) == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.wfattn_version() >= 100
+    for st in range(5):
+        assert lib.wfattn_status_string(st)
+    assert lib.wfattn_status_string(99) == b"unknown status"
+
+
+def _prefill(lib, **kw):
+    args = dict(dtype=_lib.DTYPE_F32, b=1, h=1, sq=4, sk=4, d=4, q=16, k=16, v=16, o=16,
+                scale=0.0, causal=1)
+    args.update(kw)
+    return lib.wfattn_prefill(args["dtype"], args["b"], args["h"], args["sq"], args["sk"],
+                              args["d"], args["q"], None, args["k"], None, args["v"], None,
+                              args["o"], None, args["scale"], args["causal"], None)
+
+
+@pytest.mark.parametrize("kw", [
+    {"q": None}, {"o": None}, {"b": 0}, {"sq": 0}, {"d": 0}, {"sk": 3, "sq": 4},
+    {"scale": float("nan")},
+])
+def test_prefill_rejects_bad_arguments_on_host(kw):
+    lib = _lib.load()
+    assert _prefill(lib, **kw) == _lib.INVALID_ARG
+    assert lib.wfattn_last_error()
+
+
+def test_reference_abi_rejects_foreign_geometry_on_host():
+    lib = _lib.load()
+    bad = _lib.Dim3(3, 1, 1)
+    good = _lib.Dim3(4, 1, 1)
+    st = lib.wfattn_attention(16, 16, 16, 16, 4, 4, ctypes.byref(bad), ctypes.byref(good), None)
+    assert st == _lib.INVALID_ARG
+    assert b"grid" in lib.wfattn_last_error()
+    st = lib.wfattn_attention(16, 16, 16, 16, 4, 4, ctypes.byref(good), ctypes.byref(bad), None)
+    assert st == _lib.INVALID_ARG
+    assert lib.wfattn_attention(16, 16, 16, 16, 0, 4, None, None, None) == _lib.INVALID_ARG
+
+
+def test_decode_rejects_bad_arguments_on_host():
+    lib = _lib.load()
+    ws = lib.wfattn_decode_workspace_size(2, 3, 1000, 64)
+    assert ws == 2 * 3 * 4 * 66 * 4
+    assert lib.wfattn_decode_workspace_size(0, 3, 1000, 64) == 0
+    # missing workspace
+    st = lib.wfattn_decode(2, 3, 64, 1000, 16, None, 16, None, 16, None, 16, 16, None, 0.0,
+                           None, 0, None)
+    assert st == _lib.INVALID_ARG
+    # unsupported head_dim
+    st = lib.wfattn_decode(2, 3, 32, 1000, 16, None, 16, None, 16, None, 16, 16, None, 0.0,
+                           16, 1 << 20, None)
+    assert st == _lib.UNSUPPORTED
+
+
+def test_check_raises_with_library_message():
+    lib = _lib.load()
+    with pytest.raises(_lib.WfattnError, match="INVALID_ARG"):
+        _lib.check(_prefill(lib, b=0))

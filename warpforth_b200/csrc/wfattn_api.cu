@@ -1,0 +1,275 @@
+// wfattn_api.cu -- the C ABI of libwfattn (include/wfattn.h): argument
+// validation, per-device setup, dispatch to the kernels, error reporting.
+//
+// Error behaviour follows the reference's contract where it has one (the
+// caller owns every buffer, launches are asynchronous, the kernel allocates
+// nothing) and replaces its `exit(1)` on failure
+// (tools/warpforth-runner/warpforth-runner.cpp:28-38) with status codes.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/wfattn.h"
+#include "wfattn_internal.h"
+
+namespace wfattn {
+
+// One status word per device.  Kernels OR bits into it when a bounded wait
+// expires; wfattn_device_status() reads and clears it.
+__device__ unsigned int g_device_status;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+std::mutex g_dev_mutex;
+std::vector<DeviceInfo> g_devices;  // indexed by device ordinal; sm_count == 0 means unset
+
+wfattn_status_t fail(wfattn_status_t st, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return st;
+}
+
+wfattn_status_t cuda_fail(cudaError_t err, const char *what) {
+  return fail(WFATTN_CUDA_ERROR, "%s: %s (%s)", what, cudaGetErrorName(err),
+              cudaGetErrorString(err));
+}
+
+// Looks up (and on first use sets up) the properties of the current device.
+wfattn_status_t current_device(DeviceInfo *out) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if ((int)g_devices.size() <= dev) g_devices.resize(dev + 1, DeviceInfo{});
+  DeviceInfo &d = g_devices[dev];
+  if (d.sm_count == 0) {
+    cudaDeviceProp prop;
+    err = cudaGetDeviceProperties(&prop, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetDeviceProperties");
+    void *status = nullptr;
+    err = cudaGetSymbolAddress(&status, g_device_status);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(status)");
+    d.device = dev;
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    d.smem_optin = prop.sharedMemPerBlockOptin;
+    d.status = static_cast<unsigned int *>(status);
+    d.sm_count = prop.multiProcessorCount;
+  }
+  *out = d;
+  return WFATTN_OK;
+}
+
+bool is_sm100(const DeviceInfo &d) { return d.cc_major == 10 && d.cc_minor == 0; }
+
+Strides3 resolve_strides(const int64_t *s, int64_t H, int64_t S, int64_t D) {
+  if (s) return Strides3{s[0], s[1], s[2]};
+  return Strides3{H * S * D, S * D, D};
+}
+
+bool strides_ok(const Strides3 &s) { return s.b >= 0 && s.h >= 0 && s.s >= 0; }
+
+float resolve_scale(float scale, int64_t D) {
+  return scale > 0.f ? scale : (float)(1.0 / sqrt((double)D));
+}
+
+}  // namespace
+}  // namespace wfattn
+
+using namespace wfattn;
+
+extern "C" {
+
+int wfattn_version(void) { return 100; }
+
+const char *wfattn_status_string(wfattn_status_t status) {
+  switch (status) {
+    case WFATTN_OK: return "ok";
+    case WFATTN_INVALID_ARG: return "invalid argument";
+    case WFATTN_UNSUPPORTED: return "unsupported";
+    case WFATTN_CUDA_ERROR: return "cuda error";
+    case WFATTN_TIMEOUT: return "device wait timed out";
+  }
+  return "unknown status";
+}
+
+const char *wfattn_last_error(void) { return t_last_error.c_str(); }
+
+wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t seq_q,
+                               int64_t seq_k, int64_t head_dim, const void *q,
+                               const int64_t *q_strides, const void *k, const int64_t *k_strides,
+                               const void *v, const int64_t *v_strides, void *o,
+                               const int64_t *o_strides, float scale, int causal, void *stream) {
+  t_last_error.clear();
+  if (!q || !k || !v || !o) return fail(WFATTN_INVALID_ARG, "null tensor pointer");
+  if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 || head_dim < 1)
+    return fail(WFATTN_INVALID_ARG, "sizes must be >= 1 (B=%lld H=%lld Sq=%lld Sk=%lld D=%lld)",
+                (long long)batch, (long long)heads, (long long)seq_q, (long long)seq_k,
+                (long long)head_dim);
+  if (causal && seq_k < seq_q)
+    return fail(WFATTN_INVALID_ARG, "causal attention needs seq_k >= seq_q (%lld < %lld)",
+                (long long)seq_k, (long long)seq_q);
+  if (!(scale == scale)) return fail(WFATTN_INVALID_ARG, "scale is NaN");
+  PrefillArgs a;
+  a.B = batch;
+  a.H = heads;
+  a.Sq = seq_q;
+  a.Sk = seq_k;
+  a.D = head_dim;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.o = o;
+  a.qs = resolve_strides(q_strides, heads, seq_q, head_dim);
+  a.ks = resolve_strides(k_strides, heads, seq_k, head_dim);
+  a.vs = resolve_strides(v_strides, heads, seq_k, head_dim);
+  a.os = resolve_strides(o_strides, heads, seq_q, head_dim);
+  if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os))
+    return fail(WFATTN_INVALID_ARG, "negative stride");
+  a.scale = resolve_scale(scale, head_dim);
+  a.causal = causal ? 1 : 0;
+
+  DeviceInfo dev;
+  wfattn_status_t st = current_device(&dev);
+  if (st != WFATTN_OK) return st;
+  if (!is_sm100(dev))
+    return fail(WFATTN_UNSUPPORTED, "libwfattn is built for sm_100a; device %d is sm_%d%d",
+                dev.device, dev.cc_major, dev.cc_minor);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err;
+  if (dtype == WFATTN_DTYPE_F32) {
+    if (head_dim > 256) return fail(WFATTN_UNSUPPORTED, "f32 path supports head_dim <= 256");
+    err = launch_prefill_f32(a, dev, s);
+    if (err != cudaSuccess) return cuda_fail(err, "prefill_f32 launch");
+    return WFATTN_OK;
+  }
+  if (dtype == WFATTN_DTYPE_BF16) {
+    if (head_dim != 64) return fail(WFATTN_UNSUPPORTED, "bf16 path supports head_dim == 64 only");
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!al16(q) || !al16(k) || !al16(v) || !al16(o))
+      return fail(WFATTN_INVALID_ARG, "bf16 tensors must be 16-byte aligned");
+    const Strides3 *all[4] = {&a.qs, &a.ks, &a.vs, &a.os};
+    for (const Strides3 *x : all)
+      if (x->b % 8 || x->h % 8 || x->s % 8)
+        return fail(WFATTN_INVALID_ARG, "bf16 strides must be multiples of 8 elements");
+    err = launch_prefill_bf16(a, dev, s);
+    if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
+    return WFATTN_OK;
+  }
+  return fail(WFATTN_INVALID_ARG, "unknown dtype %d", dtype);
+}
+
+wfattn_status_t wfattn_attention(const float *Q, const float *K, const float *V, float *O,
+                                 int64_t seq_len, int64_t head_dim, const wfattn_dim3 *grid,
+                                 const wfattn_dim3 *block, void *stream) {
+  t_last_error.clear();
+  if (seq_len < 1 || head_dim < 1)
+    return fail(WFATTN_INVALID_ARG, "SEQ_LEN and HEAD_DIM must be >= 1 (got %lld, %lld)",
+                (long long)seq_len, (long long)head_dim);
+  auto is_ref_geom = [seq_len](const wfattn_dim3 *g) {
+    return g->x == (unsigned long long)seq_len && g->y == 1 && g->z == 1;
+  };
+  if (grid && !is_ref_geom(grid))
+    return fail(WFATTN_INVALID_ARG, "grid (%u,%u,%u) is not the kernel's (SEQ_LEN,1,1)", grid->x,
+                grid->y, grid->z);
+  if (block && !is_ref_geom(block))
+    return fail(WFATTN_INVALID_ARG, "block (%u,%u,%u) is not the kernel's (SEQ_LEN,1,1)",
+                block->x, block->y, block->z);
+  return wfattn_prefill(WFATTN_DTYPE_F32, 1, 1, seq_len, seq_len, head_dim, Q, nullptr, K,
+                        nullptr, V, nullptr, O, nullptr, 0.f, 1, stream);
+}
+
+size_t wfattn_decode_workspace_size(int64_t batch, int64_t heads, int64_t max_kv_len,
+                                    int64_t head_dim) {
+  if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1) return 0;
+  return decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
+}
+
+wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, int64_t max_kv_len,
+                              const void *q, const int64_t *q_strides, const void *k_cache,
+                              const int64_t *k_strides, const void *v_cache,
+                              const int64_t *v_strides, const int32_t *kv_lens, float *o,
+                              const int64_t *o_strides, float scale, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  t_last_error.clear();
+  if (!q || !k_cache || !v_cache || !kv_lens || !o)
+    return fail(WFATTN_INVALID_ARG, "null tensor pointer");
+  if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1)
+    return fail(WFATTN_INVALID_ARG, "sizes must be >= 1");
+  if (head_dim != 64) return fail(WFATTN_UNSUPPORTED, "decode supports head_dim == 64 only");
+  const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
+  if (!workspace || workspace_bytes < need)
+    return fail(WFATTN_INVALID_ARG, "workspace of %zu bytes needed, %zu given", need,
+                workspace ? workspace_bytes : (size_t)0);
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(o) || !al16(workspace))
+    return fail(WFATTN_INVALID_ARG, "decode tensors and workspace must be 16-byte aligned");
+  DecodeArgs a;
+  a.B = batch;
+  a.H = heads;
+  a.D = head_dim;
+  a.max_len = max_kv_len;
+  a.q = q;
+  a.qs = q_strides ? Strides3{q_strides[0], q_strides[1], 0} : Strides3{heads * head_dim, head_dim, 0};
+  a.k = k_cache;
+  a.v = v_cache;
+  a.ks = resolve_strides(k_strides, heads, max_kv_len, head_dim);
+  a.vs = resolve_strides(v_strides, heads, max_kv_len, head_dim);
+  a.kv_lens = kv_lens;
+  a.o = o;
+  a.os = o_strides ? Strides3{o_strides[0], o_strides[1], 0} : Strides3{heads * head_dim, head_dim, 0};
+  a.scale = resolve_scale(scale, head_dim);
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os))
+    return fail(WFATTN_INVALID_ARG, "negative stride");
+  if (a.qs.b % 8 || a.qs.h % 8 || a.ks.b % 8 || a.ks.h % 8 || a.ks.s % 8 || a.vs.b % 8 ||
+      a.vs.h % 8 || a.vs.s % 8)
+    return fail(WFATTN_INVALID_ARG, "bf16 q/k/v strides must be multiples of 8 elements");
+  if (a.ks.s != head_dim || a.vs.s != head_dim)
+    return fail(WFATTN_UNSUPPORTED, "decode needs contiguous cache rows (seq stride == head_dim)");
+  if (a.os.b % 4 || a.os.h % 4)
+    return fail(WFATTN_INVALID_ARG, "f32 output strides must be multiples of 4 elements");
+  DeviceInfo dev;
+  wfattn_status_t st = current_device(&dev);
+  if (st != WFATTN_OK) return st;
+  if (!is_sm100(dev))
+    return fail(WFATTN_UNSUPPORTED, "libwfattn is built for sm_100a; device %d is sm_%d%d",
+                dev.device, dev.cc_major, dev.cc_minor);
+  cudaError_t err = launch_decode_bf16(a, dev, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "decode launch");
+  return WFATTN_OK;
+}
+
+wfattn_status_t wfattn_device_status(void *stream, int clear) {
+  t_last_error.clear();
+  cudaError_t err = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "cudaStreamSynchronize");
+  unsigned int word = 0;
+  err = cudaMemcpyFromSymbol(&word, g_device_status, sizeof(word));
+  if (err != cudaSuccess) return cuda_fail(err, "read device status");
+  if (clear && word) {
+    const unsigned int zero = 0;
+    err = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero));
+    if (err != cudaSuccess) return cuda_fail(err, "clear device status");
+  }
+  if (word & kDevTimeoutMask)
+    return fail(WFATTN_TIMEOUT, "a kernel's bounded wait expired (status word 0x%x)", word);
+  if (word & kDevBadLengthMask)
+    return fail(WFATTN_INVALID_ARG, "a kv_lens entry was outside [1, max_kv_len] (status 0x%x)",
+                word);
+  return WFATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,61 @@
+// Internal launch interface between the C ABI layer (wfattn_api.cu) and the
+// kernel translation units.  Every launcher returns a cudaError_t from the
+// launch; argument validation has already happened in the API layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wfattn {
+
+// Device-side status bits written by kernels whose bounded waits expired.
+enum DeviceStatusBits : unsigned int {
+  kDevTimeoutMask = 1u,
+  kDevBadLengthMask = 2u,  // a device-side length (decode kv_lens) was out of range
+};
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// Strided [B, H, S, D] view (element strides, unit head_dim stride).
+struct Strides3 {
+  int64_t b, h, s;
+};
+
+struct PrefillArgs {
+  int64_t B, H, Sq, Sk, D;
+  const void *q, *k, *v;
+  void *o;
+  Strides3 qs, ks, vs, os;
+  float scale;  // already resolved (> 0)
+  int causal;
+};
+
+struct DecodeArgs {
+  int64_t B, H, D, max_len;
+  const void *q;  // bf16 [B, H, D]
+  Strides3 qs;    // s unused
+  const void *k, *v;
+  Strides3 ks, vs;
+  const int32_t *kv_lens;
+  float *o;     // f32 [B, H, D]
+  Strides3 os;  // s unused
+  float scale;
+  void *workspace;
+  size_t workspace_bytes;
+};
+
+struct DeviceInfo {
+  int device;
+  int sm_count;
+  int cc_major, cc_minor;
+  size_t smem_optin;
+  unsigned int *status;  // device address of the status word
+};
+
+cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream);
+cudaError_t launch_prefill_bf16(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream);
+
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t D);
+cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream);
+
+}  // namespace wfattn

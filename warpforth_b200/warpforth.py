@@ -1,0 +1,164 @@
+"""Python binding of libwfattn for PyTorch tensors.
+
+``AttentionKernel`` keeps the interface of the reference's PyCUDA wrapper
+(demo/warpforth.py:16-49 in tetsuo-cpp/warpforth): construct it, then call it
+with contiguous f32 CUDA tensors ``q, k, v, o`` of shape (seq_len, head_dim)
+plus ``seq_len`` and ``head_dim``; ``o`` is overwritten with the causal
+attention of that one head.  Instead of loading ``attention.ptx`` it calls
+``wfattn_attention`` from libwfattn on torch's current stream.
+
+``attention`` and ``decode`` are the batched forms (all batches and heads in
+one launch, strided views accepted, f32 or bf16).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+from . import _lib
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+class AttentionKernel:
+    """Launches the causal attention kernel for one head (drop-in for demo/warpforth.py).
+
+    The kernel computes ``O = softmax(Q @ K^T / sqrt(head_dim)) @ V`` with a
+    causal mask, reading and writing f32.  ``ptx_path`` is accepted for
+    signature compatibility with the reference wrapper and is not read: the
+    kernel comes from libwfattn.
+    """
+
+    def __init__(self, ptx_path: str | Path | None = None) -> None:
+        self._lib = _lib.load()
+        self.ptx_path = ptx_path
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                 seq_len: int, head_dim: int) -> None:
+        for name, t in (("q", q), ("k", k), ("v", v), ("o", o)):
+            _require_cuda(name, t)
+            if t.dtype != torch.float32:
+                raise ValueError(f"{name} must be float32, got {t.dtype}")
+            if not t.is_contiguous():
+                raise ValueError(f"{name} must be contiguous")
+            if t.numel() < seq_len * head_dim:
+                raise ValueError(f"{name} holds {t.numel()} elements, fewer than "
+                                 f"seq_len*head_dim = {seq_len * head_dim}")
+        geom = _lib.Dim3(int(seq_len), 1, 1)
+        _lib.check(self._lib.wfattn_attention(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(o), int(seq_len), int(head_dim),
+            ctypes.byref(geom), ctypes.byref(geom), _stream_handle(q.device)))
+
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
+              scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Batched scaled-dot-product attention over [B, H, S, D] CUDA tensors.
+
+    q is [B, H, Sq, D], k and v are [B, H, Sk, D]; any batch/head/seq strides
+    are accepted (the head_dim stride must be 1).  f32 tensors run the
+    reference-accurate CUDA-core kernel (head_dim <= 256); bf16 tensors run
+    the tcgen05 tensor-core kernel (head_dim 64).  Causal masking aligns the
+    queries with the end of the keys.  Returns ``out`` (allocated as a
+    contiguous [B, H, Sq, D] tensor of q's dtype when not given).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t)
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be [B, H, S, D], got shape {tuple(t.shape)}")
+        if t.stride(3) != 1:
+            raise ValueError(f"{name} must have a unit head_dim stride")
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError(f"q/k/v must all be float32 or all bfloat16 (got {q.dtype}, {k.dtype}, "
+                         f"{v.dtype})")
+    b, h, sq, d = q.shape
+    sk = k.shape[2]
+    if k.shape != (b, h, sk, d) or v.shape != (b, h, sk, d):
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, "
+                         f"v {tuple(v.shape)}")
+    if out is None:
+        out = torch.empty((b, h, sq, d), dtype=q.dtype, device=q.device)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.stride(3) != 1:
+        raise ValueError("out must match q's shape and dtype with a unit head_dim stride")
+    lib = _lib.load()
+    st = [_lib.strides_arg(t.stride()[:3]) for t in (q, k, v, out)]
+    _lib.check(lib.wfattn_prefill(
+        _DTYPES[q.dtype], b, h, sq, sk, d, _ptr(q), st[0], _ptr(k), st[1], _ptr(v), st[2],
+        _ptr(out), st[3], float(scale) if scale else 0.0, 1 if causal else 0,
+        _stream_handle(q.device)))
+    return out
+
+
+class DecodeWorkspace:
+    """Caller-owned scratch for ``decode`` (grown on demand, reused across calls)."""
+
+    def __init__(self) -> None:
+        self.buffer: torch.Tensor | None = None
+
+    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        if self.buffer is None or self.buffer.numel() < nbytes or self.buffer.device != device:
+            self.buffer = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
+        return self.buffer
+
+
+def decode_workspace_size(batch: int, heads: int, max_kv_len: int, head_dim: int) -> int:
+    return int(_lib.load().wfattn_decode_workspace_size(batch, heads, max_kv_len, head_dim))
+
+
+def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_lens: torch.Tensor,
+           *, scale: float | None = None, out: torch.Tensor | None = None,
+           workspace: DecodeWorkspace | None = None) -> torch.Tensor:
+    """One-token decode attention over a padded bf16 KV cache (split-KV).
+
+    q: bf16 [B, H, D] or [B, H, 1, D]; k_cache / v_cache: bf16 [B, H, Lmax, D]
+    with contiguous rows; kv_lens: int32 CUDA [B] with 1 <= kv_lens[b] <= Lmax.
+    Returns f32 [B, H, D].
+    """
+    if q.dim() == 4:
+        q = q[:, :, 0, :]
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("kv_lens", kv_lens)):
+        _require_cuda(name, t)
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or \
+            v_cache.dtype != torch.bfloat16:
+        raise ValueError("decode expects bfloat16 q / k_cache / v_cache")
+    if kv_lens.dtype != torch.int32:
+        raise ValueError("kv_lens must be int32")
+    b, h, d = q.shape
+    lmax = k_cache.shape[2]
+    if k_cache.shape != (b, h, lmax, d) or v_cache.shape != (b, h, lmax, d):
+        raise ValueError("cache shape mismatch")
+    if out is None:
+        out = torch.empty((b, h, d), dtype=torch.float32, device=q.device)
+    ws = (workspace or DecodeWorkspace()).get(decode_workspace_size(b, h, lmax, d), q.device)
+    lib = _lib.load()
+    qs = _lib.strides_arg(q.stride()[:2])
+    ks = _lib.strides_arg(k_cache.stride()[:3])
+    vs = _lib.strides_arg(v_cache.stride()[:3])
+    os_ = _lib.strides_arg(out.stride()[:2])
+    _lib.check(lib.wfattn_decode(
+        b, h, d, lmax, _ptr(q), qs, _ptr(k_cache), ks, _ptr(v_cache), vs, _ptr(kv_lens),
+        _ptr(out), os_, float(scale) if scale else 0.0, _ptr(ws), ws.numel(),
+        _stream_handle(q.device)))
+    return out
+
+
+def device_status(clear: bool = True) -> None:
+    """Raise if a kernel on the current device recorded a device-side failure."""
+    lib = _lib.load()
+    _lib.check(lib.wfattn_device_status(_stream_handle(torch.device("cuda")), 1 if clear else 0))

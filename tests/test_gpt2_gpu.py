@@ -1,0 +1,84 @@
+"""GPT-2 end to end with every attention routed through libwfattn (the demo's caller).
+
+Random-init GPT-2 small (seed 1), a 32-token prompt (seed 1), greedy
+generation with use_cache=False as in demo/gpt2_generate.py:80-90.  The
+patched model must produce the same token ids as the stock eager model on the
+GPU and on the CPU; a difference is only accepted where the stock model's top
+two logits are within 1e-4 (a genuine tie that f32 rounding may break either
+way).
+"""
+
+from __future__ import annotations
+
+import pytest
+
+torch = pytest.importorskip("torch")
+pytest.importorskip("transformers")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def gpt2():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from warpforth_b200 import gpt2
+
+    return gpt2
+
+
+def _assert_same_or_tie(model, ids_a, ids_b, prompt_len):
+    a, b = ids_a[0].tolist(), ids_b[0].tolist()
+    assert len(a) == len(b)
+    if a == b:
+        return
+    p = next(i for i in range(len(a)) if a[i] != b[i])
+    assert p >= prompt_len
+    with torch.no_grad():
+        logits = model(ids_a[:, :p].to(next(model.parameters()).device)).logits[0, -1].float()
+    top2 = torch.topk(logits, 2).values
+    assert float(top2[0] - top2[1]) < 1e-4, f"tokens diverge at {p} without a tie"
+
+
+def test_gpt2_generation_matches_stock_eager(gpt2):
+    model = gpt2.random_gpt2(seed=1, device="cuda")
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    stock = gpt2.generate(model, prompt, 128, use_cache=False)
+    restore = gpt2.patch_gpt2()
+    try:
+        patched = gpt2.generate(model, prompt, 128, use_cache=False)
+        # logits of the full final sequence agree to f32 rounding
+        with torch.no_grad():
+            lp = model(patched).logits
+        restore()
+        with torch.no_grad():
+            ls = model(patched).logits
+    finally:
+        restore()
+    assert patched.shape[1] == 32 + 128
+    _assert_same_or_tie(model, stock, patched, 32)
+    assert float((lp - ls).abs().max()) <= 1e-3
+
+
+def test_gpt2_generation_with_kv_cache(gpt2):
+    model = gpt2.random_gpt2(seed=1, device="cuda")
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    stock = gpt2.generate(model, prompt, 64, use_cache=True)
+    restore = gpt2.patch_gpt2()
+    try:
+        patched = gpt2.generate(model, prompt, 64, use_cache=True)
+    finally:
+        restore()
+    _assert_same_or_tie(model, stock, patched, 32)
+
+
+def test_gpt2_generation_matches_cpu_run(gpt2):
+    cpu_model = gpt2.random_gpt2(seed=1, device="cpu")
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    cpu_ids = gpt2.generate(cpu_model, prompt, 128, use_cache=False)
+    model = gpt2.random_gpt2(seed=1, device="cuda")
+    restore = gpt2.patch_gpt2()
+    try:
+        gpu_ids = gpt2.generate(model, prompt, 128, use_cache=False).cpu()
+    finally:
+        restore()
+    _assert_same_or_tie(cpu_model, cpu_ids, gpu_ids, 32)

@@ -1,0 +1,123 @@
+"""Head-sharded prefill with an all-gather of O, on CPU ranks over gloo.
+
+Each rank computes only its heads (here with the CPU oracle standing in for
+the GPU kernel) into its slot of the head-major gather buffer; after the
+in-place all-gather every rank must hold the full [B, H, S, D] output,
+identical to a single-process computation.  Also covers the failure paths on
+the host: a rank that raises before the collective makes the others' gather
+fail with the group timeout instead of hanging.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+from conftest import ROOT  # noqa: E402
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _oracle_compute(q, k, v, *, causal, scale, out):
+    import oracle
+
+    res = oracle.attention(q.contiguous().numpy(), k.contiguous().numpy(),
+                           v.contiguous().numpy(), causal=causal, scale=scale)
+    out.copy_(torch.from_numpy(res))
+    return out
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(4)
+    return tuple(torch.randn(2, 6, 40, 16, generator=g) for _ in range(3))
+
+
+def _worker(rank, world, port, result_path, mode):
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=10))
+    from warpforth_b200.sharded import ShardedPrefill
+
+    q, k, v = _inputs()
+    sp = ShardedPrefill(2, 6, 40, 16, dtype=torch.float32, device=torch.device("cpu"),
+                        compute=_oracle_compute)
+    status = "ok"
+    try:
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("rank 1 fails before the collective")
+        out = sp(sp.shard(q), sp.shard(k), sp.shard(v))
+        np.save(f"{result_path}.{rank}.npy", out.contiguous().numpy())
+    except RuntimeError as e:
+        status = f"error: {e}"
+    with open(f"{result_path}.{rank}.status", "w") as f:
+        f.write(status)
+    if mode != "fail":
+        dist.destroy_process_group()
+
+
+def _spawn(world, tmp_path, mode):
+    port = _free_port()
+    path = str(tmp_path / "res")
+    mp.start_processes(_worker, args=(world, port, path, mode), nprocs=world, join=True,
+                       start_method="spawn")
+    return path
+
+
+def test_head_range_even_split():
+    from warpforth_b200.sharded import head_range
+
+    assert [head_range(48, 8, r) for r in range(8)] == [(6 * r, 6 * r + 6) for r in range(8)]
+    assert head_range(12, 1, 0) == (0, 12)
+    with pytest.raises(ValueError):
+        head_range(48, 5, 0)
+    with pytest.raises(ValueError):
+        head_range(48, 2, 2)
+
+
+def test_sharded_gather_matches_single_process(tmp_path):
+    import oracle
+
+    path = _spawn(2, tmp_path, "ok")
+    q, k, v = _inputs()
+    ref = oracle.attention(q.numpy(), k.numpy(), v.numpy())
+    for r in range(2):
+        assert open(f"{path}.{r}.status").read() == "ok"
+        out = np.load(f"{path}.{r}.npy")
+        assert out.shape == (2, 6, 40, 16)
+        assert np.array_equal(out, ref)
+
+
+def test_single_rank_output_view_is_full_tensor():
+    from warpforth_b200.sharded import ShardedPrefill
+
+    q, k, v = _inputs()
+    sp = ShardedPrefill(2, 6, 40, 16, dtype=torch.float32, device=torch.device("cpu"),
+                        compute=_oracle_compute)
+    out = sp(sp.shard(q), sp.shard(k), sp.shard(v))
+    import oracle
+
+    assert np.array_equal(out.contiguous().numpy(), oracle.attention(q.numpy(), k.numpy(),
+                                                                     v.numpy()))
+    assert out.data_ptr() == sp.gathered.data_ptr()  # a view, not a copy
+
+
+def test_failed_rank_surfaces_as_collective_error(tmp_path):
+    path = _spawn(2, tmp_path, "fail")
+    assert open(f"{path}.1.status").read().startswith("error: rank 1 fails")
+    st0 = open(f"{path}.0.status").read()
+    assert st0.startswith("error:"), st0

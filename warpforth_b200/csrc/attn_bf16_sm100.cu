@@ -22,10 +22,10 @@
 // issued heaviest-first.  Ragged edges (S not a multiple of 128) rely on TMA
 // zero fill plus an explicit key mask.
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <math.h>
 
 #include "sm100_ptx.cuh"
+#include "tma_map.h"
 #include "wfattn_internal.h"
 
 namespace wfattn {
@@ -346,45 +346,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void *sym = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(sym);
-  }
-  return fn;
-}
-
-// [B, H, S, 64] bf16 view with element strides -> 4-D tensor map, 64x128 box,
-// 128-byte swizzle, zero fill out of bounds.
-bool make_map(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
-              const Strides3 &st) {
-  auto enc = get_encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)st.s * 2, (cuuint64_t)st.h * 2, (cuuint64_t)st.b * 2};
-  // Degenerate dimensions still need a legal (multiple of 16, non-zero) stride.
-  for (int i = 0; i < 3; ++i)
-    if (strides[i] == 0) strides[i] = 16;
-  cuuint32_t box[4] = {(cuuint32_t)kD, (cuuint32_t)kBN, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 }  // namespace
 
-cudaError_t launch_prefill_bf16(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
+cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,
+                                   cudaStream_t stream) {
   static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM must fit");
   CUtensorMap tq, tk, tv;
-  if (!make_map(&tq, a.q, a.B, a.H, a.Sq, a.qs) || !make_map(&tk, a.k, a.B, a.H, a.Sk, a.ks) ||
-      !make_map(&tv, a.v, a.B, a.H, a.Sk, a.vs))
+  if (!make_bf16_map_64x128(&tq, a.q, a.B, a.H, a.Sq, a.qs) ||
+      !make_bf16_map_64x128(&tk, a.k, a.B, a.H, a.Sk, a.ks) ||
+      !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(

@@ -9,6 +9,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <mutex>
 #include <string>
@@ -163,7 +164,17 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
     for (const Strides3 *x : all)
       if (x->b % 8 || x->h % 8 || x->s % 8)
         return fail(WFATTN_INVALID_ARG, "bf16 strides must be multiples of 8 elements");
-    err = launch_prefill_bf16(a, dev, s);
+    const int64_t ext_q[3] = {batch, heads, seq_q}, ext_k[3] = {batch, heads, seq_k};
+    for (int i = 0; i < 3; ++i) {
+      const int64_t sq[3] = {a.qs.b, a.qs.h, a.qs.s}, sk[3] = {a.ks.b, a.ks.h, a.ks.s},
+                    sv[3] = {a.vs.b, a.vs.h, a.vs.s};
+      if ((ext_q[i] > 1 && sq[i] == 0) || (ext_k[i] > 1 && (sk[i] == 0 || sv[i] == 0)))
+        return fail(WFATTN_INVALID_ARG, "bf16 path does not take zero (broadcast) strides");
+    }
+    // The two-tile kernel is the default; WFATTN_PREFILL_1Q=1 selects the
+    // one-tile kernel (kept for comparison measurements).
+    static const bool one_tile = getenv("WFATTN_PREFILL_1Q") != nullptr;
+    err = one_tile ? launch_prefill_bf16_1q(a, dev, s) : launch_prefill_bf16_2q(a, dev, s);
     if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
     return WFATTN_OK;
   }

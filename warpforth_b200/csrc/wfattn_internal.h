@@ -53,7 +53,12 @@ struct DeviceInfo {
 };
 
 cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream);
-cudaError_t launch_prefill_bf16(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream);
+// bf16 prefill: one 128-row query tile per CTA (2 CTAs per SM) ...
+cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,
+                                   cudaStream_t stream);
+// ... or two 128-row tiles per CTA sharing K/V (1 CTA per SM).
+cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
+                                   cudaStream_t stream);
 
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t D);
 cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream);

@@ -68,6 +68,10 @@ WORKLOADS = {
                             "causal prefill [8,12,1024,64] f32 (reference-accurate path)"),
     "decode": Workload("decode", "decode", 64, 25, 4096, 64, 3, "bf16", False,
                        "decode q_len=1, B=64 H=25 D=64, bf16 KV cache, kv_lens~U[512,4096]"),
+    # S = new tokens per step
+    "gpt2": Workload("gpt2", "gpt2", 1, 12, 128, 64, 1, "f32", False,
+                     "GPT-2 small random-init (seed 1), 32-token prompt (seed 1), greedy 128 "
+                     "new tokens, use_cache=False, every attention through libwfattn (f32)"),
 }
 
 
@@ -166,6 +170,8 @@ def cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
 
     import oracle
 
+    if w.kind == "gpt2":
+        return gpt2_cpu_sample(target_s, threads)
     g = torch.Generator().manual_seed(w.seed)
 
     def bf(t):
@@ -237,8 +243,8 @@ def run_reference(args, w: Workload) -> None:
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": hib, "dtype": "f64", "data": "synthetic",
-        "config": config_of(w, args.gpus),
+        "higher_is_better": hib, "dtype": "f32" if w.kind == "gpt2" else "f64",
+        "data": "synthetic", "config": config_of(w, args.gpus),
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -250,12 +256,20 @@ def run_reference(args, w: Workload) -> None:
 def metric_of(w: Workload) -> tuple[str, str, bool]:
     if w.kind == "decode":
         return "decode attention KV GB/s per B200", "GB/s", True
+    if w.kind == "gpt2":
+        return "GPT-2 gen tokens/s", "tokens/s", True
     return "causal SDPA TFLOP/s", "TFLOP/s", True
 
 
 def config_of(w: Workload, n: int) -> dict:
     cfg = {"workload": w.description, "batch": w.B, "heads": w.H, "head_dim": w.D,
            "seed": w.seed}
+    if w.kind == "gpt2":
+        cfg.update({"model": "gpt2-small (12 layers, d_model 768, vocab 50257, ctx 1024)",
+                    "prompt_len": 32, "new_tokens": w.S, "use_cache": False,
+                    "parallelism": f"replicas/{n}" if n > 1 else "single",
+                    "l2": "not applicable (end-to-end generation)"})
+        return cfg
     if w.kind == "prefill":
         cfg.update({"seq_len": w.S, "causal": True,
                     "parallelism": f"heads/{n}" if w.sharded and n > 1 else
@@ -290,7 +304,147 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args, w)
         return
+    if w.kind == "gpt2":
+        run_gpt2(args, w)
+        return
     run_gpu(args, w)
+
+
+def gpt2_cpu_sample(target_s: float, threads: int) -> dict:
+    """Stock eager GPT-2 on the host cores (the demo's torch attention), greedy tokens/s."""
+    import torch
+
+    from warpforth_b200 import gpt2
+
+    torch.set_num_threads(threads)
+    model = gpt2.random_gpt2(seed=1, device="cpu")
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    n = 4
+    while True:
+        t0 = time.perf_counter()
+        gpt2.generate(model, prompt, n, use_cache=False)
+        dt = time.perf_counter() - t0
+        if dt >= 0.5 * target_s or n >= 128:
+            break
+        n = min(128, max(n + 1, int(n * min(8.0, target_s / max(dt, 1e-3)))))
+    return {"value": n / dt, "unit": "tokens/s", "seconds": dt,
+            "sample": f"stock eager GPT-2 (torch CPU, {threads} threads): the first {n} greedy "
+                      f"tokens of the same prompt in {dt:.2f} s"}
+
+
+def run_gpt2(args, w: Workload) -> None:
+    """GPT-2 generation tokens/s with every attention through libwfattn (one process per GPU)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from warpforth_b200 import gpt2
+
+    model = gpt2.random_gpt2(seed=1, device=dev)
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    prompt_dev = prompt.to(dev)
+    restore = gpt2.patch_gpt2()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        gpt2.generate(model, prompt_dev, w.S)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(physical_gpu_indices(world)) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ids = gpt2.generate(model, prompt_dev, w.S)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop() if clocks else None
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    assert ids.shape[1] == 32 + w.S
+    value = w.S * world / (ms / 1e3)
+
+    # end to end: prompt from (pinned) host memory, ids read back, inside the timed region
+    host_prompt = prompt.pin_memory()
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        out = gpt2.generate(model, host_prompt.to(dev, non_blocking=True), w.S).cpu()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    restore()
+
+    # the attention kernel at the step's largest call, [1, 12, 159, 64] f32, on its own
+    from warpforth_b200 import warpforth as wf
+
+    s_max = 32 + w.S - 1
+    q, k, v = (torch.randn(1, 12, s_max, 64, device=dev) for _ in range(3))
+    o = torch.empty_like(q)
+    for _ in range(10):
+        wf.attention(q, k, v, out=o)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(100):
+        wf.attention(q, k, v, out=o)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    kms = a0.elapsed_time(a1) / 100
+    kflops = 4 * 64 * 12 * (s_max * (s_max + 1) // 2)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = gpt2_cpu_sample(args.cpu_seconds, os.cpu_count() or 1)
+        cpu = {"value": r["value"], "unit": r["unit"], "cores": os.cpu_count(),
+               "kind": "port", "sample": r["sample"]}
+    if rank == 0:
+        peak = 148 * 128 * 2 * 1965e6 / 1e12
+        achieved = kflops / (kms / 1e3) / 1e12
+        line = {
+            "metric": "GPT-2 gen tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random-init weights, random prompt ids)",
+            "config": config_of(w, world),
+            "roofline": {"bound": "launch/latency (attention is a small part of a GPT-2 step)",
+                         "kernel": "prefill_f32_kernel at [1,12,159,64]",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "kernel_ms": kms, "traffic": None,
+                         "peak_source": "nominal f32 FMA rate at max SM clock"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": w.S * world / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "ms_per_step": e2e_ms, "steps": e2e_steps,
+                    "h2d_bytes_per_step": prompt.numel() * prompt.element_size(),
+                    "d2h_bytes_per_step": out.numel() * out.element_size(),
+                    "path": "transformers generate -> patched eager_attention_forward -> "
+                            "libwfattn"},
+            "gpu_launches": args.steps * world * 12 * w.S,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_gpu(args, w: Workload) -> None:

@@ -296,11 +296,20 @@ def main() -> None:
     ap.add_argument("--ref-step-seconds", type=float, default=4.0,
                     help="target CPU time of one reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--shape", default=None,
+                    help="B,H,S override of a prefill workload (profiling a smaller case)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     w = WORKLOADS[args.workload]
+    if args.shape:
+        b, h, s = (int(x) for x in args.shape.split(","))
+        if w.kind != "prefill":
+            ap.error("--shape applies to prefill workloads only")
+        w = Workload(w.name, w.kind, b, h, s, w.D, w.seed, w.dtype, w.sharded,
+                     f"causal prefill [{b},{h},{s},{w.D}] {w.dtype} (shape override of "
+                     f"{w.name})")
     if args.impl == "reference":
         run_reference(args, w)
         return

@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (ptx::timeout_flagged(p.status)) return;  // sticky until the host clears it
+  if (threadIdx.x == 0) trace(0, 1);
 
   const int64_t BH = p.B * p.H;
   const int64_t qp = p.n_pairs - 1 - (int64_t)blockIdx.x / BH;  // heaviest first
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(ptx::smem_u32(&sm.drain), 1);
     sm.abort = 0;
     ptx::fence_barrier_init();
+    trace(0, 2);
   }
   if (warp == 8 && lane == 0) {
     ptx::prefetch_tmap(&tm_q);
@@ -162,13 +164,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tm_v);
   }
   if (warp == 9) {
+    if (lane == 0) trace(1, 1);
     ptx::tmem_alloc(ptx::smem_u32(&sm.tmem_base), kTmemCols);
     ptx::tmem_relinquish();
+    if (lane == 0) trace(1, 2);
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  if (threadIdx.x == 0) {
+    trace(0, 3);
+    trace(7, tmem);
+  }
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
@@ -178,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive_expect_tx(qf, kTileBytes * nq);
       for (int t = 0; t < nq; ++t)
         ptx::tma_load_4d(ptx::smem_u32(sm.q[t]), &tm_q, 0, (int)(q0 + t * kBM), h, b, qf);
+      trace(2, 1);
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_kv && !aborted(sm); ++j) {
         const int st = j % kStages;
@@ -200,7 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_arrive_expect_tx(vf, kTileBytes);
         ptx::tma_load_4d(ptx::smem_u32(sm.v[st]), &tm_v, 0, j * kBN, h, b, vf);
         issued_v = j + 1;
+        trace(2, 100 + j);
       }
+      trace(2, aborted(sm) ? 6 : 5);
       if (aborted(sm)) {
         ptx::mbar_wait_drain(qf, 0);
         for (int i = (int)imin64(issued_k, kStages); i > 0; --i) {
@@ -219,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(kBM, kD, 0, 1);
       bool ok = ptx::mbar_wait(ptx::smem_u32(&sm.q_full), 0, p.status);
+      trace(1, ok ? 3 : 4);
 
       auto issue_pv = [&](int i) -> bool {
         const int st = i % kStages;
@@ -240,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_commit(ptx::smem_u32(&sm.o_done[t]));
         }
         ptx::tc_commit(ptx::smem_u32(&sm.v_empty[st]));
+        trace(1, 10000 + i);
         return true;
       };
 
@@ -272,12 +285,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         ptx::tc_commit(ptx::smem_u32(&sm.k_empty[st]));
+        trace(1, 100 + j);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
           break;
         }
       }
       if (ok) ok = issue_pv(n_kv - 1);
+      trace(1, ok ? 5 : 6);
       if (!ok) {
         set_abort(sm);
         ptx::tc_commit(ptx::smem_u32(&sm.drain));
@@ -389,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar_p_full);
+      if (row == 0) trace(3 + t, 100 + j);
     }
     if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(n - 1) & 1, p.status));
     if (ok) {
@@ -414,17 +430,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (n > 0) {
       set_abort(sm);
     }
+    if (row == 0) trace(3 + t, ok ? 5 : 6);
   }
 
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace(6, 1);
   if (warp == 9) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
+    if (lane == 0) trace(1, 8);
   }
 }
 
 }  // namespace
+
+#ifdef WFATTN_TRACE
+cudaError_t set_trace_prefill_2q(void *p) { return set_trace_symbol(p); }
+#endif
 
 cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
                                    cudaStream_t stream) {

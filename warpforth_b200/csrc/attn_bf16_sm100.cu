@@ -82,6 +82,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // A timeout recorded by an earlier launch is sticky until the host clears it.
   if (ptx::timeout_flagged(p.status)) return;
+  if (threadIdx.x == 0) trace(0, 1);
 
   const int64_t BH = p.B * p.H;
   const int64_t qt = p.n_qtiles - 1 - (int64_t)blockIdx.x / BH;  // heaviest first
@@ -116,13 +117,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     ptx::prefetch_tmap(&tm_v);
   }
   if (warp == 5) {
+    if (lane == 0) trace(1, 1);
     ptx::tmem_alloc(ptx::smem_u32(&sm.tmem_base), kTmemCols);
     ptx::tmem_relinquish();
+    if (lane == 0) trace(1, 2);
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  if (threadIdx.x == 0) {
+    trace(0, 3);
+    trace(7, tmem);
+  }
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
@@ -152,7 +159,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         ptx::mbar_arrive_expect_tx(vf, kTileBytes);
         ptx::tma_load_4d(ptx::smem_u32(sm.v[st]), &tm_v, 0, j * kBN, h, b, vf);
         issued_v = j + 1;
+        trace(2, 100 + j);
       }
+      trace(2, aborted(sm) ? 6 : 5);
       if (aborted(sm)) {
         // Drain: every load this thread issued must land before the CTA exits.
         ptx::mbar_wait_drain(qf, 0);
@@ -174,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t tS = tmem + kColS, tP = tmem + kColP, tO = tmem + kColO;
       const uint32_t q_addr = ptx::smem_u32(sm.q);
       bool ok = ptx::mbar_wait(ptx::smem_u32(&sm.q_full), 0, p.status);
+      trace(1, ok ? 3 : 4);
 
       auto issue_pv = [&](int i) -> bool {
         const int st = i % kStages;
@@ -221,6 +231,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (ok) ok = issue_pv(n_kv - 1);
+      trace(1, ok ? 5 : 6);
       if (!ok) {
         set_abort(sm);
         // Drain: wait until every MMA this thread issued has completed.
@@ -308,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(ptx::smem_u32(&sm.p_full));
+      if (row == 0) trace(3, 100 + j);
     }
     if (ok) {
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(ptx::smem_u32(&sm.o_done),
@@ -338,15 +350,22 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
+  if (threadIdx.x == 0) trace(3, 5);
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace(6, 1);
   if (warp == 5) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
+    if (lane == 0) trace(1, 8);
   }
 }
 
 }  // namespace
+
+#ifdef WFATTN_TRACE
+cudaError_t set_trace_prefill_1q(void *p) { return set_trace_symbol(p); }
+#endif
 
 cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,
                                    cudaStream_t stream) {

@@ -106,19 +106,26 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecParams 
     for (int i = 0; i < 8; ++i) qf[i] *= p.scale_log2;
   }
 
-  bool ok = ptx::mbar_wait(bar_k, 0, p.status);
-  // ---- scores: keys t = 4*warp + sub + 16*i
-  for (int t = warp * 4 + sub; ok && t < n; t += 16) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(sm.k + t * kRowBytes + g * 16);
-    float kf[8];
-    bf16x8_to_f32(w, kf);
+  // CTA-uniform outcome: every thread takes the same path through the
+  // barriers and full-warp shuffles below.
+  bool ok = __syncthreads_and(ptx::mbar_wait(bar_k, 0, p.status)) != 0;
+  // ---- scores: keys t = 4*warp + sub + 16*i.  The loop bound depends on the
+  // warp only, so all 32 lanes run the same iterations and reach every
+  // full-mask shuffle together; lanes past the end of the chunk just idle.
+  for (int base = warp * 4; ok && base < n; base += 16) {
+    const int t = base + sub;
     float d = 0.f;
+    if (t < n) {
+      const uint4 w = *reinterpret_cast<const uint4 *>(sm.k + t * kRowBytes + g * 16);
+      float kf[8];
+      bf16x8_to_f32(w, kf);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) d = fmaf(qf[i], kf[i], d);
+      for (int i = 0; i < 8; ++i) d = fmaf(qf[i], kf[i], d);
+    }
     d += __shfl_xor_sync(0xffffffffu, d, 1);
     d += __shfl_xor_sync(0xffffffffu, d, 2);
     d += __shfl_xor_sync(0xffffffffu, d, 4);
-    if (g == 0) sm.s[t] = d;
+    if (g == 0 && t < n) sm.s[t] = d;
   }
   __syncthreads();
 
@@ -142,7 +149,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecParams 
   __syncthreads();
 
   // ---- P.V
-  ok = ok && ptx::mbar_wait(bar_v, 0, p.status);
+  ok = __syncthreads_and(ok && ptx::mbar_wait(bar_v, 0, p.status)) != 0;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;

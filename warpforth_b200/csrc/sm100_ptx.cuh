@@ -15,6 +15,26 @@
 #include "wfattn_internal.h"
 
 namespace wfattn {
+
+#ifdef WFATTN_TRACE
+// Debug builds only (-DWFATTN_TRACE): per-CTA progress words in host-mapped
+// memory, readable by the host while a kernel is still running.  Slot s of
+// CTA c is trace[c * 8 + s].  Each translation unit has its own pointer,
+// set through its set_trace_* host function.
+static __device__ unsigned int *g_trace;
+static inline cudaError_t set_trace_symbol(void *p) {
+  return cudaMemcpyToSymbol(g_trace, &p, sizeof(p));
+}
+__device__ __forceinline__ void trace(int slot, unsigned int v) {
+  if (g_trace) {
+    *reinterpret_cast<volatile unsigned int *>(&g_trace[blockIdx.x * 8 + slot]) = v;
+    __threadfence_system();
+  }
+}
+#else
+__device__ __forceinline__ void trace(int, unsigned int) {}
+#endif
+
 namespace ptx {
 
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s

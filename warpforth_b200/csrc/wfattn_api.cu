@@ -86,6 +86,11 @@ float resolve_scale(float scale, int64_t D) {
 }
 
 }  // namespace
+
+#ifdef WFATTN_TRACE
+cudaError_t set_trace_prefill_1q(void *p);
+cudaError_t set_trace_prefill_2q(void *p);
+#endif
 }  // namespace wfattn
 
 using namespace wfattn;
@@ -262,6 +267,18 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
   if (err != cudaSuccess) return cuda_fail(err, "decode launch");
   return WFATTN_OK;
 }
+
+#ifdef WFATTN_TRACE
+// Debug builds only: route the kernels' progress trace to `host_mapped`
+// (cudaHostAllocMapped memory of at least 8 words per CTA), or NULL to stop.
+__attribute__((visibility("default"))) int wfattn_debug_set_trace(void *host_mapped) {
+  void *dev = nullptr;
+  if (host_mapped && cudaHostGetDevicePointer(&dev, host_mapped, 0) != cudaSuccess) return 1;
+  if (set_trace_prefill_1q(dev) != cudaSuccess) return 2;
+  if (set_trace_prefill_2q(dev) != cudaSuccess) return 3;
+  return 0;
+}
+#endif
 
 wfattn_status_t wfattn_device_status(void *stream, int clear) {
   t_last_error.clear();

@@ -136,6 +136,35 @@ WFATTN_API wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t h
                               size_t workspace_bytes, void *stream);
 
 /*
+ * Decode without any device allocation -- no counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: code that only holds the buffers it
+ * was handed (a plugin whose host framework owns all device memory through
+ * its own pool, or a foreign-language caller with no CUDA allocator of its
+ * own), and decode loops that cannot afford the device synchronisation an
+ * allocation may cause.  Same arguments and results as wfattn_decode, minus
+ * the workspace: the split-KV partials live in a static device array of
+ * 8 MiB (8,388,608 bytes) inside the library, which every GPU that loads the
+ * library holds until the process exits.  Shapes needing more scratch than
+ * that -- batch * heads * ceil(max_kv_len / 256) above 31,775 -- are rejected
+ * with WFATTN_INVALID_ARG before any CUDA call.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All calls
+ * share the one array: calls that overlap on the GPU (e.g. on two streams)
+ * race and must be serialised by the caller.  Nothing in the array needs to
+ * start at zero; each call writes every partial it reads.
+ */
+WFATTN_API wfattn_status_t wfattn_decode_noalloc(int64_t batch, int64_t heads, int64_t head_dim,
+                                                 int64_t max_kv_len, const void *q,
+                                                 const int64_t *q_strides, const void *k_cache,
+                                                 const int64_t *k_strides, const void *v_cache,
+                                                 const int64_t *v_strides,
+                                                 const int32_t *kv_lens, float *o,
+                                                 const int64_t *o_strides, float scale,
+                                                 void *stream);
+
+/*
  * Reads (and optionally clears) the device-side status word of the current
  * device: WFATTN_OK, or WFATTN_TIMEOUT when a bounded wait inside a kernel
  * (TMA/MMA pipeline barrier) gave up and the kernel returned early.

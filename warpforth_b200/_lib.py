@@ -19,7 +19,8 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 
 EXPORTED_SYMBOLS = (
     "wfattn_version", "wfattn_status_string", "wfattn_last_error", "wfattn_attention",
-    "wfattn_prefill", "wfattn_decode_workspace_size", "wfattn_decode", "wfattn_device_status",
+    "wfattn_prefill", "wfattn_decode_workspace_size", "wfattn_decode", "wfattn_decode_noalloc",
+    "wfattn_device_status",
 )
 
 
@@ -65,6 +66,9 @@ def load() -> ctypes.CDLL:
     lib.wfattn_decode.restype = ctypes.c_int
     lib.wfattn_decode.argtypes = [_i64, _i64, _i64, _i64, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                                   _vp, _vp, _i64p, ctypes.c_float, _vp, ctypes.c_size_t, _vp]
+    lib.wfattn_decode_noalloc.restype = ctypes.c_int
+    lib.wfattn_decode_noalloc.argtypes = [_i64, _i64, _i64, _i64, _vp, _i64p, _vp, _i64p, _vp,
+                                          _i64p, _vp, _vp, _i64p, ctypes.c_float, _vp]
     lib.wfattn_device_status.restype = ctypes.c_int
     lib.wfattn_device_status.argtypes = [_vp, ctypes.c_int]
     _lib = lib

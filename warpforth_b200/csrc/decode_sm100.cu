@@ -17,6 +17,9 @@
 // transfer (separate barriers), and ~3 CTAs per SM keep loads in flight.
 #include <math.h>
 
+#include <mutex>
+#include <vector>
+
 #include "sm100_ptx.cuh"
 #include "wfattn_internal.h"
 
@@ -224,7 +227,35 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams
   *reinterpret_cast<float2 *>(dst + 2 * lane) = make_float2(o0 * inv, o1 * inv);
 }
 
+std::mutex g_scratch_mutex;
+std::vector<void *> g_scratch_addr;  // per device ordinal; nullptr until set up
+
 }  // namespace
+
+// Scratch of the allocation-free decode entry point: a file-scope device
+// array, so the library never has to call cudaMalloc for it.  Every device
+// that loads this module holds it until the process exits.
+static __device__ __align__(256) unsigned char g_decode_scratch[kDecodeNoAllocScratchBytes];
+
+// Device address of g_decode_scratch on the current device.  Host code cannot
+// pass the symbol itself to a kernel (on the host it names a host-side
+// stand-in), so the address is looked up once per device, with that device
+// current, and cached.
+cudaError_t decode_noalloc_scratch(void **ptr) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if ((int)g_scratch_addr.size() <= dev) g_scratch_addr.resize(dev + 1, nullptr);
+  if (!g_scratch_addr[dev]) {
+    void *addr = nullptr;
+    err = cudaGetSymbolAddress(&addr, g_decode_scratch);
+    if (err != cudaSuccess) return err;
+    g_scratch_addr[dev] = addr;
+  }
+  *ptr = g_scratch_addr[dev];
+  return cudaSuccess;
+}
 
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t) {
   const int64_t nch = (max_len + kChunk - 1) / kChunk;

@@ -268,6 +268,36 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
   return WFATTN_OK;
 }
 
+// Decode for callers that cannot allocate device memory: the split-KV
+// partials go to a static device array instead of a caller workspace, then
+// the ordinary decode path runs on it.  Checks the size against the array
+// before any CUDA call; looks the array's address up on the first call per
+// device (with that device current).
+wfattn_status_t wfattn_decode_noalloc(int64_t batch, int64_t heads, int64_t head_dim,
+                                      int64_t max_kv_len, const void *q,
+                                      const int64_t *q_strides, const void *k_cache,
+                                      const int64_t *k_strides, const void *v_cache,
+                                      const int64_t *v_strides, const int32_t *kv_lens, float *o,
+                                      const int64_t *o_strides, float scale, void *stream) {
+  t_last_error.clear();
+  if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1)
+    return fail(WFATTN_INVALID_ARG, "sizes must be >= 1");
+  const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
+  if (need > kDecodeNoAllocScratchBytes)
+    return fail(WFATTN_INVALID_ARG,
+                "wfattn_decode_noalloc: this shape needs %zu bytes of scratch but the static "
+                "scratch holds %zu (batch*heads*ceil(max_kv_len/256) must be <= %zu); use "
+                "wfattn_decode with a caller workspace",
+                need, kDecodeNoAllocScratchBytes,
+                kDecodeNoAllocScratchBytes / (size_t)((64 + 2) * sizeof(float)));
+  void *scratch = nullptr;
+  const cudaError_t err = decode_noalloc_scratch(&scratch);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(decode scratch)");
+  return wfattn_decode(batch, heads, head_dim, max_kv_len, q, q_strides, k_cache, k_strides,
+                       v_cache, v_strides, kv_lens, o, o_strides, scale, scratch,
+                       kDecodeNoAllocScratchBytes, stream);
+}
+
 #ifdef WFATTN_TRACE
 // Debug builds only: route the kernels' progress trace to `host_mapped`
 // (cudaHostAllocMapped memory of at least 8 words per CTA), or NULL to stop.

@@ -63,4 +63,9 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t D);
 cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream);
 
+// Size of the static device scratch behind wfattn_decode_noalloc (8 MiB).
+constexpr size_t kDecodeNoAllocScratchBytes = size_t(8) << 20;
+// Device address of that scratch on the current device (looked up on first use).
+cudaError_t decode_noalloc_scratch(void **ptr);
+
 }  // namespace wfattn

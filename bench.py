@@ -733,15 +733,18 @@ def run_e2e(args, w, world, rank, dev, tdt, barrier, max_over_ranks, wf, sp, uni
 
 
 def load_traffic(w: Workload):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "traffic.json"
+    """DRAM bytes per launch of the dominant kernel from profiles/traffic.md, if captured."""
+    p = ROOT / "profiles" / "traffic.md"
     if not p.exists():
         return None
-    try:
-        data = json.loads(p.read_text())
-    except ValueError:
-        return None
-    return data.get(w.name)
+    for line in p.read_text().splitlines():
+        cells = [c.strip() for c in line.strip().strip("|").split("|")]
+        if len(cells) >= 3 and cells[0] == w.name:
+            try:
+                return int(cells[2])
+            except ValueError:
+                return None
+    return None
 
 
 if __name__ == "__main__":

@@ -2,15 +2,26 @@
 // accumulation on tcgen05 tensor cores; two 128-row query tiles per CTA.
 //
 // One CTA (one per SM) computes 256 query rows of one (batch, head) as two
-// 128-row tiles A and B that share every K/V tile loaded by TMA, which halves
-// the L2 -> shared-memory traffic per FLOP compared with one tile per CTA.
+// 128-row tiles A and B that share every K/V tile loaded by TMA (half the
+// L2 -> shared-memory traffic per FLOP of one tile per CTA).
 //
-//   warp 8 (TMA)     Q_A, Q_B once; then K_j, V_j 128x64 tiles into a ring
-//   warp 9 (MMA)     S_A = Q_A K_j^T, S_B = Q_B K_j^T        (SS form)
-//                    O_A += P_A V_{j-1}, O_B += P_B V_{j-1}  (TS form, P from TMEM)
-//   warps 0-3 / 4-7  softmax of tile A / tile B: thread r owns query row r,
-//                    reads S from TMEM, writes bf16 P to TMEM, rescales its O
-//                    row in TMEM when needed, and stores the normalised row.
+//   warp 16 (TMA, K)  Q_A, Q_B once; then K_j tiles into a 4-deep ring
+//   warp 18 (TMA, V)  V_j tiles into their own 4-deep ring.  K and V have
+//                     separate producers so a K load never waits for a V
+//                     slot (V slots free only after P.V, much later than K
+//                     slots free after Q.K^T); this keeps the K loads far
+//                     enough ahead that their latency is off the critical path.
+//   warp 17 (MMA)     S_A = Q_A K_j^T, S_B = Q_B K_j^T        (SS form)
+//                     O_A += P_A V_{j-1}, O_B += P_B V_{j-1}  (TS form, P from TMEM)
+//                     issued with precomputed descriptors (few instructions
+//                     per MMA; this warp shares a scheduler with softmax warps)
+//   warps 0-7 / 8-15  softmax of tile A / tile B.  Warp w reads the 16 rows
+//                     32*(w%4) + 16*((w/4)%2) + [0,16) of its tile with the
+//                     16x256b TMEM shape: each row is held by one quad of
+//                     lanes (32 columns each), so the row max and row sum
+//                     need two quad shuffles and no cross-warp barrier, and
+//                     every thread holds whole bf16 column pairs of P, which
+//                     it packs and stores (16x128b shape) without exchanges.
 //
 // TMEM (512 columns): S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384)
 //                     O_A [384,448) O_B [448,512).
@@ -22,11 +33,11 @@
 //    rare steps;
 //  * scale-and-subtract, sums and rescales use packed f32x2 FMA/ADD/MUL, the
 //    row max uses the three-input max;
-//  * kPolyPairsOf8 of every 8 exponential pairs are evaluated on the FMA pipes with the
-//    Cody-Waite + minimax polynomial of exp2_poly.cuh (relative error 7.5e-5,
-//    below the bf16 rounding of P), the rest on the MUFU ex2 unit; the two
-//    units then run in parallel.  Masked (diagonal / ragged) tiles use MUFU
-//    only.
+//  * kPolyPairsOf8 of every 8 exponential pairs are evaluated on the FMA
+//    pipes with the Cody-Waite + minimax polynomial of exp2_poly.cuh
+//    (relative error 7.5e-5, below the bf16 rounding of P), the rest on the
+//    MUFU ex2 unit (16 results/clock/SM on B200), so both run in parallel.
+//    Masked (diagonal / ragged) tiles use MUFU only.
 #include <cuda.h>
 #include <math.h>
 
@@ -41,8 +52,10 @@ namespace {
 constexpr int kBM = 128;  // rows per query tile (= TMEM lanes)
 constexpr int kBN = 128;  // keys per K/V tile
 constexpr int kD = 64;
-constexpr int kStages = 3;
-constexpr int kThreads = 320;  // 8 softmax warps + TMA warp + MMA warp
+constexpr int kStages = 4;
+constexpr int kSoftmaxWarps = 16;  // 2 tiles x 8 warps of 16 rows
+constexpr int kTmaKWarp = 16, kMmaWarp = 17, kTmaVWarp = 18;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 3);
 constexpr uint32_t kTileBytes = kBN * kD * 2;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColP0 = 256, kColO0 = 384;  // tile t: + 128t / 64t / 64t
@@ -58,6 +71,9 @@ struct Smem {
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
   uint64_t drain;
+#ifdef WFATTN_TRACE
+  unsigned long long tl[24][64];  // cycle timeline of CTA 0 (trace builds only)
+#endif
   uint32_t tmem_base;
   uint32_t abort;
 };
@@ -72,6 +88,17 @@ struct Params {
   int causal;
   unsigned int *status;
 };
+
+#ifdef WFATTN_TRACE
+#define TL(e, j)                                                  \
+  do {                                                            \
+    if (blockIdx.x == 0 && (j) < 64) sm.tl[(e)][(j)] = clock64(); \
+  } while (0)
+#else
+#define TL(e, j) \
+  do {           \
+  } while (0)
+#endif
 
 __device__ __forceinline__ bool aborted(const Smem &s) {
   return *reinterpret_cast<const volatile uint32_t *>(&s.abort) != 0;
@@ -109,6 +136,15 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
   float x0, x1;
   ptx::f2_unpack(x2, x0, x1);
   return ptx::f2_pack(ptx::ex2_approx(x0), ptx::ex2_approx(x1));
+}
+
+__device__ __forceinline__ float quad_max(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+}
+__device__ __forceinline__ float quad_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  return x + __shfl_xor_sync(0xffffffffu, x, 2);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -158,17 +194,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::fence_barrier_init();
     trace(0, 2);
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == kTmaKWarp && lane == 0) {
     ptx::prefetch_tmap(&tm_q);
     ptx::prefetch_tmap(&tm_k);
-    ptx::prefetch_tmap(&tm_v);
   }
-  if (warp == 9) {
+  if (warp == kTmaVWarp && lane == 0) ptx::prefetch_tmap(&tm_v);
+  if (warp == kMmaWarp) {
     if (lane == 0) trace(1, 1);
     ptx::tmem_alloc(ptx::smem_u32(&sm.tmem_base), kTmemCols);
     ptx::tmem_relinquish();
     if (lane == 0) trace(1, 2);
   }
+#ifdef WFATTN_TRACE
+  for (int i = threadIdx.x; i < 24 * 64; i += kThreads) (&sm.tl[0][0])[i] = 0ull;
+#endif
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -178,57 +217,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     trace(7, tmem);
   }
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == kTmaKWarp || warp == kTmaVWarp) {
+    // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
+      const bool is_k = warp == kTmaKWarp;
+      const CUtensorMap *tm = is_k ? &tm_k : &tm_v;
+      uint64_t *full = is_k ? sm.k_full : sm.v_full;
+      uint64_t *empty = is_k ? sm.k_empty : sm.v_empty;
+      uint8_t(*ring)[kTileBytes] = is_k ? sm.k : sm.v;
       const uint32_t qf = ptx::smem_u32(&sm.q_full);
-      const int nq = qrows[1] > 0 ? 2 : 1;
-      ptx::mbar_arrive_expect_tx(qf, kTileBytes * nq);
-      for (int t = 0; t < nq; ++t)
-        ptx::tma_load_4d(ptx::smem_u32(sm.q[t]), &tm_q, 0, (int)(q0 + t * kBM), h, b, qf);
+      if (is_k) {
+        const int nq = qrows[1] > 0 ? 2 : 1;
+        ptx::mbar_arrive_expect_tx(qf, kTileBytes * nq);
+        for (int t = 0; t < nq; ++t)
+          ptx::tma_load_4d(ptx::smem_u32(sm.q[t]), &tm_q, 0, (int)(q0 + t * kBM), h, b, qf);
+      }
       trace(2, 1);
-      int issued_k = 0, issued_v = 0;
+      int issued = 0;  // loads issued so far (tile index + 1)
       for (int j = 0; j < n_kv && !aborted(sm); ++j) {
         const int st = j % kStages;
         const uint32_t use = (uint32_t)(j / kStages);
         if (j >= kStages &&
-            !ptx::mbar_wait(ptx::smem_u32(&sm.k_empty[st]), (use - 1) & 1, p.status)) {
+            !ptx::mbar_wait(ptx::smem_u32(&empty[st]), (use - 1) & 1, p.status)) {
           set_abort(sm);
           break;
         }
-        const uint32_t kf = ptx::smem_u32(&sm.k_full[st]);
-        ptx::mbar_arrive_expect_tx(kf, kTileBytes);
-        ptx::tma_load_4d(ptx::smem_u32(sm.k[st]), &tm_k, 0, j * kBN, h, b, kf);
-        issued_k = j + 1;
-        if (j >= kStages &&
-            !ptx::mbar_wait(ptx::smem_u32(&sm.v_empty[st]), (use - 1) & 1, p.status)) {
-          set_abort(sm);
-          break;
-        }
-        const uint32_t vf = ptx::smem_u32(&sm.v_full[st]);
-        ptx::mbar_arrive_expect_tx(vf, kTileBytes);
-        ptx::tma_load_4d(ptx::smem_u32(sm.v[st]), &tm_v, 0, j * kBN, h, b, vf);
-        issued_v = j + 1;
-        trace(2, 100 + j);
+        const uint32_t fb = ptx::smem_u32(&full[st]);
+        ptx::mbar_arrive_expect_tx(fb, kTileBytes);
+        ptx::tma_load_4d(ptx::smem_u32(ring[st]), tm, 0, j * kBN, h, b, fb);
+        issued = j + 1;
+        if (is_k) TL(10, j);
       }
-      trace(2, aborted(sm) ? 6 : 5);
       if (aborted(sm)) {
-        ptx::mbar_wait_drain(qf, 0);
-        for (int i = (int)imin64(issued_k, kStages); i > 0; --i) {
-          const int t = issued_k - i;
-          ptx::mbar_wait_drain(ptx::smem_u32(&sm.k_full[t % kStages]), (uint32_t)(t / kStages) & 1);
-        }
-        for (int i = (int)imin64(issued_v, kStages); i > 0; --i) {
-          const int t = issued_v - i;
-          ptx::mbar_wait_drain(ptx::smem_u32(&sm.v_full[t % kStages]), (uint32_t)(t / kStages) & 1);
+        // Drain: every load this thread issued must land before the CTA exits.
+        if (is_k) ptx::mbar_wait_drain(qf, 0);
+        for (int i = (int)imin64(issued, kStages); i > 0; --i) {
+          const int t = issued - i;
+          ptx::mbar_wait_drain(ptx::smem_u32(&full[t % kStages]), (uint32_t)(t / kStages) & 1);
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(kBM, kD, 0, 1);
+      // Descriptors: constant high halves; low halves = start address >> 4
+      // (a K step adds 32 B for Q/K, 2 KB for V; a ring stage adds 16 KB).
+      const uint64_t dq0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.q[0]), 16, 1024);
+      const uint64_t dq1 = ptx::smem_desc_sw128(ptx::smem_u32(sm.q[1]), 16, 1024);
+      const uint64_t dk0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.k[0]), 16, 1024);
+      const uint64_t dv0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.v[0]), kTileBytes, 1024);
+      const uint32_t hi_qk = (uint32_t)(dk0 >> 32), hi_v = (uint32_t)(dv0 >> 32);
+      const uint32_t qlo[2] = {(uint32_t)dq0, (uint32_t)dq1};
+      const uint32_t klo0 = (uint32_t)dk0, vlo0 = (uint32_t)dv0;
+      constexpr uint32_t kStageLo = kTileBytes >> 4;
       bool ok = ptx::mbar_wait(ptx::smem_u32(&sm.q_full), 0, p.status);
       trace(1, ok ? 3 : 4);
 
@@ -236,7 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = i % kStages;
         if (!ptx::mbar_wait(ptx::smem_u32(&sm.v_full[st]), (uint32_t)(i / kStages) & 1, p.status))
           return false;
-        const uint32_t v_addr = ptx::smem_u32(sm.v[st]);
+        TL(18, i);
+        const uint32_t vb = vlo0 + st * kStageLo;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (i >= nkv[t]) continue;
@@ -244,12 +288,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             return false;
           ptx::tc_fence_after();
           const uint32_t tO = tmem + kColO0 + 64 * t, tP = tmem + kColP0 + 64 * t;
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t bd = ptx::smem_desc_sw128(v_addr + kk * 2048, kTileBytes, 1024);
-            ptx::mma_ts(tO, tP + kk * 8, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-          }
+          if (i == 0)
+            ptx::mma_ts_lh<false>(tO, tP, vb, hi_v, idesc_pv);
+          else
+            ptx::mma_ts_lh<true>(tO, tP, vb, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 8, vb + 128, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 16, vb + 256, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 24, vb + 384, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 32, vb + 512, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 40, vb + 640, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 48, vb + 768, hi_v, idesc_pv);
+          ptx::mma_ts_lh<true>(tO, tP + 56, vb + 896, hi_v, idesc_pv);
           ptx::tc_commit(ptx::smem_u32(&sm.o_done[t]));
+          TL(2 + t, i);
         }
         ptx::tc_commit(ptx::smem_u32(&sm.v_empty[st]));
         trace(1, 10000 + i);
@@ -263,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const uint32_t k_addr = ptx::smem_u32(sm.k[st]);
+        TL(17, j);
+        const uint32_t kb = klo0 + st * kStageLo;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j >= nkv[t]) continue;
@@ -273,15 +325,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t q_addr = ptx::smem_u32(sm.q[t]);
-          const uint32_t tS = tmem + kColS0 + 128 * t;
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint64_t ad = ptx::smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-            const uint64_t bd = ptx::smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-            ptx::mma_ss(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-          }
+          const uint32_t tS = tmem + kColS0 + 128 * t, qa = qlo[t];
+          ptx::mma_ss_lh<false>(tS, qa, hi_qk, kb, hi_qk, idesc_qk);
+          ptx::mma_ss_lh<true>(tS, qa + 2, hi_qk, kb + 2, hi_qk, idesc_qk);
+          ptx::mma_ss_lh<true>(tS, qa + 4, hi_qk, kb + 4, hi_qk, idesc_qk);
+          ptx::mma_ss_lh<true>(tS, qa + 6, hi_qk, kb + 6, hi_qk, idesc_qk);
           ptx::tc_commit(ptx::smem_u32(&sm.s_full[t]));
+          TL(t, j);
         }
         if (!ok) break;
         ptx::tc_commit(ptx::smem_u32(&sm.k_empty[st]));
@@ -295,148 +345,190 @@ __global__ void __launch_bounds__(kThreads, 1)
       trace(1, ok ? 5 : 6);
       if (!ok) {
         set_abort(sm);
+        // Drain: wait until every MMA this thread issued has completed.
         ptx::tc_commit(ptx::smem_u32(&sm.drain));
         ptx::mbar_wait_drain(ptx::smem_u32(&sm.drain), 0);
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warps 0-7
-    const int t = warp >> 2;             // query tile of this warpgroup
-    const int row = threadIdx.x & 127;   // TMEM lane == row within the tile
-    const int n = nkv[t];
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    // ------------------------------------------------------------ softmax warps 0-15
+    const int t = warp >> 3;                          // query tile
+    const int blk = 32 * (warp & 3) + 16 * ((warp >> 2) & 1);  // first row of this warp
+    const int qd = lane & 3;                          // column pair within each 8 columns
+    const int r0 = blk + (lane >> 2), r1 = r0 + 8;    // the two rows of this thread
+    const int n = t ? nkv[1] : nkv[0];
+    const int rows = t ? qrows[1] : qrows[0];
+    const uint32_t lane_base = tmem + ((uint32_t)blk << 16);
     const uint32_t cS = kColS0 + 128 * t, cP = kColP0 + 64 * t, cO = kColO0 + 64 * t;
-    const int64_t grow = q0 + t * kBM + row;
+    const int64_t g0 = q0 + t * kBM + r0, g1 = g0 + 8;  // global query rows
     const uint32_t bar_s_full = ptx::smem_u32(&sm.s_full[t]);
     const uint32_t bar_s_free = ptx::smem_u32(&sm.s_free[t]);
     const uint32_t bar_p_full = ptx::smem_u32(&sm.p_full[t]);
     const uint32_t bar_o_done = ptx::smem_u32(&sm.o_done[t]);
+    const bool arrive_lane = lane < 16;  // 16 arrivals per warp x 8 warps = 128
     const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
-    float m_run = -INFINITY, l_run = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY;  // running offsets of rows r0, r1
+    float l0 = 0.f, l1 = 0.f;              // this thread's share of the row sums
     bool ok = n > 0;
     for (int j = 0; j < n; ++j) {
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_s_full, (uint32_t)j & 1, p.status));
       if (!ok) break;
       ptx::tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) ptx::tmem_ld32(lane_base + cS + c * 32, sr[c]);
+      uint32_t sr[64];
+      ptx::tmem_ld_16x256b_x16(lane_base + cS, sr);
       ptx::tmem_wait_ld();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(bar_s_free);
+      if (arrive_lane) ptx::mbar_arrive(bar_s_free);
+      if (t == 0 && warp == 0 && lane == 0) TL(4, j);
 
       const int64_t n0 = (int64_t)j * kBN;
       const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q0 + t * kBM + off);
       if (masked) {
-        const int64_t lim = p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1;
+        const int64_t lim0 = (p.causal ? imin64(g0 + off, p.Sk - 1) : p.Sk - 1) - n0 - 2 * qd;
+        const int64_t lim1 = (p.causal ? imin64(g1 + off, p.Sk - 1) : p.Sk - 1) - n0 - 2 * qd;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int k = 0; k < 16; ++k)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (n0 + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+          for (int e = 0; e < 4; ++e)
+            if (8 * k + (e & 1) > ((e & 2) ? lim1 : lim0))
+              sr[4 * k + e] = __float_as_uint(-INFINITY);
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      float a0 = -INFINITY, a1 = -INFINITY, b0 = -INFINITY, b1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          mx0 = ptx::fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-          mx1 = ptx::fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
-          mx2 = ptx::fmax3(mx2, __uint_as_float(sr[c][e + 4]), __uint_as_float(sr[c][e + 5]));
-          mx3 = ptx::fmax3(mx3, __uint_as_float(sr[c][e + 6]), __uint_as_float(sr[c][e + 7]));
-        }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
-      float alpha = 1.f;
-      if (mx > m_run + kRescaleLog2) {  // first tile: m_run = -inf
-        alpha = ptx::ex2_approx(m_run - mx);
-        m_run = mx;
+      for (int k = 0; k < 16; k += 2) {
+        a0 = ptx::fmax3(a0, __uint_as_float(sr[4 * k]), __uint_as_float(sr[4 * k + 1]));
+        b0 = ptx::fmax3(b0, __uint_as_float(sr[4 * k + 2]), __uint_as_float(sr[4 * k + 3]));
+        a1 = ptx::fmax3(a1, __uint_as_float(sr[4 * k + 4]), __uint_as_float(sr[4 * k + 5]));
+        b1 = ptx::fmax3(b1, __uint_as_float(sr[4 * k + 6]), __uint_as_float(sr[4 * k + 7]));
       }
-      const uint64_t nm2 = ptx::f2_pack(-m_run, -m_run);
-      uint64_t sum2a = 0, sum2b = 0;  // bit pattern 0 == (0.f, 0.f)
-      uint32_t pk[2][32];
+      const float mx0 = quad_max(fmaxf(a0, a1)) * p.scale_log2;
+      const float mx1 = quad_max(fmaxf(b0, b1)) * p.scale_log2;
+      float alpha0 = 1.f, alpha1 = 1.f;
+      if (mx0 > m0 + kRescaleLog2) {  // first tile: m = -inf
+        alpha0 = ptx::ex2_approx(m0 - mx0);
+        m0 = mx0;
+      }
+      if (mx1 > m1 + kRescaleLog2) {
+        alpha1 = ptx::ex2_approx(m1 - mx1);
+        m1 = mx1;
+      }
+      const uint64_t nm0 = ptx::f2_pack(-m0, -m0), nm1 = ptx::f2_pack(-m1, -m1);
+      uint64_t s0 = 0, s1 = 0;  // bit pattern 0 == (0.f, 0.f)
+      uint32_t pk[32];
+      if (masked) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int k = 0; k < 16; ++k)
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const uint64_t s2 = ptx::f2_pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-          const uint64_t x2 = ptx::f2_fma(s2, c2, nm2);
-          const bool poly = !masked && (((e & 15) >> 1) < kPolyPairsOf8);
-          const uint64_t p2 = poly ? exp2_poly2(x2) : exp2_mufu2(x2);
-          if (e & 2)
-            sum2b = ptx::f2_add(sum2b, p2);
-          else
-            sum2a = ptx::f2_add(sum2a, p2);
-          float p0, p1;
-          ptx::f2_unpack(p2, p0, p1);
-          pk[c >> 1][(c & 1) * 16 + e / 2] = ptx::pack_bf16x2(p0, p1);
-        }
-      float sa0, sa1, sb0, sb1;
-      ptx::f2_unpack(sum2a, sa0, sa1);
-      ptx::f2_unpack(sum2b, sb0, sb1);
-      l_run = l_run * alpha + ((sa0 + sa1) + (sb0 + sb1));
+          for (int v = 0; v < 2; ++v) {
+            const uint64_t x2 = ptx::f2_fma(
+                ptx::f2_pack(__uint_as_float(sr[4 * k + 2 * v]), __uint_as_float(sr[4 * k + 2 * v + 1])),
+                c2, v ? nm1 : nm0);
+            const uint64_t p2 = exp2_mufu2(x2);
+            if (v)
+              s1 = ptx::f2_add(s1, p2);
+            else
+              s0 = ptx::f2_add(s0, p2);
+            float p0, p1;
+            ptx::f2_unpack(p2, p0, p1);
+            pk[2 * k + v] = ptx::pack_bf16x2(p0, p1);
+          }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const uint64_t x2 = ptx::f2_fma(
+                ptx::f2_pack(__uint_as_float(sr[4 * k + 2 * v]), __uint_as_float(sr[4 * k + 2 * v + 1])),
+                c2, v ? nm1 : nm0);
+            const bool poly = ((2 * k + v) & 7) < kPolyPairsOf8;
+            const uint64_t p2 = poly ? exp2_poly2(x2) : exp2_mufu2(x2);
+            if (v)
+              s1 = ptx::f2_add(s1, p2);
+            else
+              s0 = ptx::f2_add(s0, p2);
+            float p0, p1;
+            ptx::f2_unpack(p2, p0, p1);
+            pk[2 * k + v] = ptx::pack_bf16x2(p0, p1);
+          }
+      }
+      float x0, x1, y0, y1;
+      ptx::f2_unpack(s0, x0, x1);
+      ptx::f2_unpack(s1, y0, y1);
+      l0 = l0 * alpha0 + (x0 + x1);
+      l1 = l1 * alpha1 + (y0 + y1);
+      if (t == 0 && warp == 0 && lane == 0) TL(6, j);
 
+      // P_j overwrites P_{j-1}: wait until P_{j-1}.V has completed (which also
+      // makes O final for the rescale).  P is stored first so its registers
+      // are free before O is loaded.
       if (j > 0) {
         ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(j - 1) & 1, p.status));
         if (!ok) break;
         ptx::tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          const uint64_t a2 = ptx::f2_pack(alpha, alpha);
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t o[32];
-            ptx::tmem_ld32(lane_base + cO + c * 32, o);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const uint64_t v2 = ptx::f2_mul(
-                  ptx::f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
-              float v0, v1;
-              ptx::f2_unpack(v2, v0, v1);
-              o[e] = __float_as_uint(v0);
-              o[e + 1] = __float_as_uint(v1);
-            }
-            ptx::tmem_st32(lane_base + cO + c * 32, o);
-          }
-        }
       }
-      ptx::tmem_st32(lane_base + cP, pk[0]);
-      ptx::tmem_st32(lane_base + cP + 32, pk[1]);
+      ptx::tmem_st_16x128b_x16(lane_base + cP, pk);
+      if (j > 0 && __any_sync(0xffffffffu, alpha0 != 1.f || alpha1 != 1.f)) {
+        uint32_t o[32];
+        ptx::tmem_ld_16x256b_x8(lane_base + cO, o);
+        ptx::tmem_wait_ld();
+        const uint64_t a20 = ptx::f2_pack(alpha0, alpha0), a21 = ptx::f2_pack(alpha1, alpha1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const uint64_t w2 = ptx::f2_mul(
+                ptx::f2_pack(__uint_as_float(o[4 * k + 2 * v]), __uint_as_float(o[4 * k + 2 * v + 1])),
+                v ? a21 : a20);
+            float w0, w1;
+            ptx::f2_unpack(w2, w0, w1);
+            o[4 * k + 2 * v] = __float_as_uint(w0);
+            o[4 * k + 2 * v + 1] = __float_as_uint(w1);
+          }
+        ptx::tmem_st_16x256b_x8(lane_base + cO, o);
+      }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(bar_p_full);
-      if (row == 0) trace(3 + t, 100 + j);
+      if (arrive_lane) ptx::mbar_arrive(bar_p_full);
+      if (t == 0 && warp == 0 && lane == 0) TL(8, j);
+      if (warp == 8 * t && lane == 0) trace(3 + t, 100 + j);
     }
     if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(n - 1) & 1, p.status));
     if (ok) {
       ptx::tc_fence_after();
-      const float inv = 1.f / l_run;
-      uint32_t o[2][32];
-      ptx::tmem_ld32(lane_base + cO, o[0]);
-      ptx::tmem_ld32(lane_base + cO + 32, o[1]);
+      const float inv0 = 1.f / quad_sum(l0), inv1 = 1.f / quad_sum(l1);
+      uint32_t o[32];
+      ptx::tmem_ld_16x256b_x8(lane_base + cO, o);
       ptx::tmem_wait_ld();
-      if (row < qrows[t]) {
-        char *dst = p.o + 2 * (b * p.os_b + h * p.os_h + grow * p.os_s);
+      char *base = p.o + 2 * (b * p.os_b + h * p.os_h) + 4 * qd;
+      if (r0 < rows) {
+        char *dst = base + 2 * g0 * p.os_s;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 w;
-          const uint32_t *src = &o[c >> 2][(c & 3) * 8];
-          w.x = ptx::pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-          w.y = ptx::pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-          w.z = ptx::pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-          w.w = ptx::pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-          reinterpret_cast<uint4 *>(dst)[c] = w;
-        }
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint32_t *>(dst + 16 * k) = ptx::pack_bf16x2(
+              __uint_as_float(o[4 * k]) * inv0, __uint_as_float(o[4 * k + 1]) * inv0);
+      }
+      if (r1 < rows) {
+        char *dst = base + 2 * g1 * p.os_s;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint32_t *>(dst + 16 * k) = ptx::pack_bf16x2(
+              __uint_as_float(o[4 * k + 2]) * inv1, __uint_as_float(o[4 * k + 3]) * inv1);
       }
     } else if (n > 0) {
       set_abort(sm);
     }
-    if (row == 0) trace(3 + t, ok ? 5 : 6);
+    if (warp == 8 * t && lane == 0) trace(3 + t, ok ? 5 : 6);
   }
 
   ptx::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) trace(6, 1);
-  if (warp == 9) {
+#ifdef WFATTN_TRACE
+  if (blockIdx.x == 0 && g_trace)
+    for (int i = threadIdx.x; i < 24 * 64; i += kThreads)
+      reinterpret_cast<volatile unsigned long long *>(g_trace + 4096)[i] = (&sm.tl[0][0])[i];
+#endif
+  if (warp == kMmaWarp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
     if (lane == 0) trace(1, 8);

@@ -5,23 +5,20 @@
 // 128-row tiles A and B that share every K/V tile loaded by TMA (half the
 // L2 -> shared-memory traffic per FLOP of one tile per CTA).
 //
-//   warp 16 (TMA, K)  Q_A, Q_B once; then K_j tiles into a 4-deep ring
-//   warp 18 (TMA, V)  V_j tiles into their own 4-deep ring.  K and V have
+//   warp 1 (TMA, K)   Q_A, Q_B once; then K_j tiles into a 4-deep ring
+//   warp 2 (TMA, V)   V_j tiles into their own 4-deep ring.  K and V have
 //                     separate producers so a K load never waits for a V
-//                     slot (V slots free only after P.V, much later than K
-//                     slots free after Q.K^T); this keeps the K loads far
-//                     enough ahead that their latency is off the critical path.
-//   warp 17 (MMA)     S_A = Q_A K_j^T, S_B = Q_B K_j^T        (SS form)
-//                     O_A += P_A V_{j-1}, O_B += P_B V_{j-1}  (TS form, P from TMEM)
-//                     issued with precomputed descriptors (few instructions
-//                     per MMA; this warp shares a scheduler with softmax warps)
-//   warps 0-7 / 8-15  softmax of tile A / tile B.  Warp w reads the 16 rows
-//                     32*(w%4) + 16*((w/4)%2) + [0,16) of its tile with the
-//                     16x256b TMEM shape: each row is held by one quad of
-//                     lanes (32 columns each), so the row max and row sum
-//                     need two quad shuffles and no cross-warp barrier, and
-//                     every thread holds whole bf16 column pairs of P, which
-//                     it packs and stores (16x128b shape) without exchanges.
+//                     slot (V slots free only after P.V, later than K slots).
+//   warp 0 (MMA, QK)  S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T, each as soon as
+//                     that tile's softmax has read S(j-1) out of TMEM, so the
+//                     next scores are computed while the softmax still works
+//   warp 3 (MMA, PV)  O_A += P_A(j) V_j, O_B += P_B(j) V_j, each as soon as that
+//                     tile's softmax has written P(j)
+//   warps 4-7 / 8-11  softmax of tile A / tile B, one query row per thread
+//                     (TMEM lane = row, 32x32b loads; warp w reads lanes
+//                     32*(w%4)..+31, the sub-partition it may access): the
+//                     row max and row sum need no shuffles and each thread
+//                     packs its own P row.
 //
 // TMEM (512 columns): S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384)
 //                     O_A [384,448) O_B [448,512).
@@ -36,8 +33,9 @@
 //  * kPolyPairsOf8 of every 8 exponential pairs are evaluated on the FMA
 //    pipes with the Cody-Waite + minimax polynomial of exp2_poly.cuh
 //    (relative error 7.5e-5, below the bf16 rounding of P), the rest on the
-//    MUFU ex2 unit (16 results/clock/SM on B200), so both run in parallel.
-//    Masked (diagonal / ragged) tiles use MUFU only.
+//    MUFU ex2 unit, so both run in parallel.  A masked score (-inf) comes
+//    out of the polynomial as 2^-126 instead of 0: against the row maximum's
+//    p >= 1 that is far below f32 resolution in both the row sum and P.V.
 #include <cuda.h>
 #include <math.h>
 
@@ -53,14 +51,15 @@ constexpr int kBM = 128;  // rows per query tile (= TMEM lanes)
 constexpr int kBN = 128;  // keys per K/V tile
 constexpr int kD = 64;
 constexpr int kStages = 4;
-constexpr int kSoftmaxWarps = 16;  // 2 tiles x 8 warps of 16 rows
-constexpr int kTmaKWarp = 16, kMmaWarp = 17, kTmaVWarp = 18;
-constexpr int kThreads = 32 * (kSoftmaxWarps + 3);
+constexpr int kSoftmaxWarps = 8;  // 2 tiles x 4 warps of 32 rows
+// Helper warps 0-3 (one per scheduler), softmax warps 4-11.
+constexpr int kMmaQkWarp = 0, kTmaKWarp = 1, kTmaVWarp = 2, kMmaPvWarp = 3, kFirstSoftmaxWarp = 4;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
 constexpr uint32_t kTileBytes = kBN * kD * 2;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColP0 = 256, kColO0 = 384;  // tile t: + 128t / 64t / 64t
 constexpr float kRescaleLog2 = 8.f;
-constexpr int kPolyPairsOf8 = 3;  // exp2 pairs per 8 pairs on the polynomial (37.5%)
+constexpr int kPolyPairsOf8 = 2;  // exp2 pairs per 8 pairs on the polynomial (25%)
 
 struct Smem {
   uint8_t q[2][kTileBytes];
@@ -70,7 +69,7 @@ struct Smem {
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
-  uint64_t drain;
+  uint64_t drain[2];  // per MMA-issuing thread
 #ifdef WFATTN_TRACE
   unsigned long long tl[24][64];  // cycle timeline of CTA 0 (trace builds only)
 #endif
@@ -138,15 +137,6 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
   return ptx::f2_pack(ptx::ex2_approx(x0), ptx::ex2_approx(x1));
 }
 
-__device__ __forceinline__ float quad_max(float x) {
-  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
-  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
-}
-__device__ __forceinline__ float quad_sum(float x) {
-  x += __shfl_xor_sync(0xffffffffu, x, 1);
-  return x + __shfl_xor_sync(0xffffffffu, x, 2);
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_bf16_2q_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_k,
@@ -189,7 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&sm.p_full[t]), kBM);
       ptx::mbar_init(ptx::smem_u32(&sm.o_done[t]), 1);
     }
-    ptx::mbar_init(ptx::smem_u32(&sm.drain), 1);
+    ptx::mbar_init(ptx::smem_u32(&sm.drain[0]), 1);
+    ptx::mbar_init(ptx::smem_u32(&sm.drain[1]), 1);
     sm.abort = 0;
     ptx::fence_barrier_init();
     trace(0, 2);
@@ -199,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tm_k);
   }
   if (warp == kTmaVWarp && lane == 0) ptx::prefetch_tmap(&tm_v);
-  if (warp == kMmaWarp) {
+  if (warp == kMmaQkWarp) {
     if (lane == 0) trace(1, 1);
     ptx::tmem_alloc(ptx::smem_u32(&sm.tmem_base), kTmemCols);
     ptx::tmem_relinquish();
@@ -246,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_arrive_expect_tx(fb, kTileBytes);
         ptx::tma_load_4d(ptx::smem_u32(ring[st]), tm, 0, j * kBN, h, b, fb);
         issued = j + 1;
-        if (is_k) TL(10, j);
+        if (is_k) TL(20, j);
       }
       if (aborted(sm)) {
         // Drain: every load this thread issued must land before the CTA exits.
@@ -257,9 +248,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kMmaQkWarp || warp == kMmaPvWarp) {
+    // ------------------------------------------------------------ MMA issuers
+    // Two threads feed the tensor core: one issues S = Q K^T, the other
+    // O += P V.  A tcgen05.mma issue stalls while the tensor pipe is busy, so
+    // one thread alone would leave the pipe idle during each of its barrier
+    // waits; with two, one waits while the other issues.
     if (lane == 0) {
+      const bool is_qk = warp == kMmaQkWarp;
       constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(kBM, kD, 0, 1);
       // Descriptors: constant high halves; low halves = start address >> 4
@@ -272,252 +268,203 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t qlo[2] = {(uint32_t)dq0, (uint32_t)dq1};
       const uint32_t klo0 = (uint32_t)dk0, vlo0 = (uint32_t)dv0;
       constexpr uint32_t kStageLo = kTileBytes >> 4;
-      bool ok = ptx::mbar_wait(ptx::smem_u32(&sm.q_full), 0, p.status);
+      bool ok = n_kv > 0 && (!is_qk || ptx::mbar_wait(ptx::smem_u32(&sm.q_full), 0, p.status));
       trace(1, ok ? 3 : 4);
 
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % kStages;
-        if (!ptx::mbar_wait(ptx::smem_u32(&sm.v_full[st]), (uint32_t)(i / kStages) & 1, p.status))
+      // S_t = Q_t K_j^T once softmax t has read S_t(j-1) out of TMEM.
+      auto issue_qk = [&](int t, int j) -> bool {
+        if (j > 0 &&
+            !ptx::mbar_wait(ptx::smem_u32(&sm.s_free[t]), (uint32_t)(j - 1) & 1, p.status))
           return false;
-        TL(18, i);
-        const uint32_t vb = vlo0 + st * kStageLo;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (i >= nkv[t]) continue;
-          if (!ptx::mbar_wait(ptx::smem_u32(&sm.p_full[t]), (uint32_t)i & 1, p.status))
-            return false;
-          ptx::tc_fence_after();
-          const uint32_t tO = tmem + kColO0 + 64 * t, tP = tmem + kColP0 + 64 * t;
-          if (i == 0)
-            ptx::mma_ts_lh<false>(tO, tP, vb, hi_v, idesc_pv);
-          else
-            ptx::mma_ts_lh<true>(tO, tP, vb, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 8, vb + 128, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 16, vb + 256, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 24, vb + 384, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 32, vb + 512, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 40, vb + 640, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 48, vb + 768, hi_v, idesc_pv);
-          ptx::mma_ts_lh<true>(tO, tP + 56, vb + 896, hi_v, idesc_pv);
-          ptx::tc_commit(ptx::smem_u32(&sm.o_done[t]));
-          TL(2 + t, i);
-        }
-        ptx::tc_commit(ptx::smem_u32(&sm.v_empty[st]));
-        trace(1, 10000 + i);
+        TL(t ? 13 : 5, j);
+        ptx::tc_fence_after();
+        const uint32_t tS = tmem + kColS0 + 128 * t, qa = qlo[t];
+        const uint32_t kb = klo0 + (j % kStages) * kStageLo;
+        ptx::mma_ss_lh<false>(tS, qa, hi_qk, kb, hi_qk, idesc_qk);
+        ptx::mma_ss_lh<true>(tS, qa + 2, hi_qk, kb + 2, hi_qk, idesc_qk);
+        ptx::mma_ss_lh<true>(tS, qa + 4, hi_qk, kb + 4, hi_qk, idesc_qk);
+        ptx::mma_ss_lh<true>(tS, qa + 6, hi_qk, kb + 6, hi_qk, idesc_qk);
+        TL(t ? 14 : 6, j);
+        ptx::tc_commit(ptx::smem_u32(&sm.s_full[t]));
+        TL(t, j);
+        return true;
+      };
+      // O_t += P_t(j) V_j once softmax t has written P_t(j) (and rescaled O_t).
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!ptx::mbar_wait(ptx::smem_u32(&sm.p_full[t]), (uint32_t)j & 1, p.status)) return false;
+        TL(t ? 15 : 9, j);
+        ptx::tc_fence_after();
+        const uint32_t tO = tmem + kColO0 + 64 * t, tP = tmem + kColP0 + 64 * t;
+        const uint32_t vb = vlo0 + (j % kStages) * kStageLo;
+        if (j == 0)
+          ptx::mma_ts_lh<false>(tO, tP, vb, hi_v, idesc_pv);
+        else
+          ptx::mma_ts_lh<true>(tO, tP, vb, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 8, vb + 128, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 16, vb + 256, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 24, vb + 384, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 32, vb + 512, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 40, vb + 640, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 48, vb + 768, hi_v, idesc_pv);
+        ptx::mma_ts_lh<true>(tO, tP + 56, vb + 896, hi_v, idesc_pv);
+        TL(t ? 17 : 11, j);
+        ptx::tc_commit(ptx::smem_u32(&sm.o_done[t]));
+        TL(2 + t, j);
         return true;
       };
 
+      uint64_t *full = is_qk ? sm.k_full : sm.v_full;
+      uint64_t *empty = is_qk ? sm.k_empty : sm.v_empty;
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j % kStages;
-        if (!ptx::mbar_wait(ptx::smem_u32(&sm.k_full[st]), (uint32_t)(j / kStages) & 1,
-                            p.status)) {
-          ok = false;
-          break;
-        }
-        TL(17, j);
-        const uint32_t kb = klo0 + st * kStageLo;
+        ok = ptx::mbar_wait(ptx::smem_u32(&full[st]), (uint32_t)(j / kStages) & 1, p.status);
+        TL(is_qk ? 18 : 19, j);
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (j >= nkv[t]) continue;
-          if (j > 0 &&
-              !ptx::mbar_wait(ptx::smem_u32(&sm.s_free[t]), (uint32_t)(j - 1) & 1, p.status)) {
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          const uint32_t tS = tmem + kColS0 + 128 * t, qa = qlo[t];
-          ptx::mma_ss_lh<false>(tS, qa, hi_qk, kb, hi_qk, idesc_qk);
-          ptx::mma_ss_lh<true>(tS, qa + 2, hi_qk, kb + 2, hi_qk, idesc_qk);
-          ptx::mma_ss_lh<true>(tS, qa + 4, hi_qk, kb + 4, hi_qk, idesc_qk);
-          ptx::mma_ss_lh<true>(tS, qa + 6, hi_qk, kb + 6, hi_qk, idesc_qk);
-          ptx::tc_commit(ptx::smem_u32(&sm.s_full[t]));
-          TL(t, j);
-        }
-        if (!ok) break;
-        ptx::tc_commit(ptx::smem_u32(&sm.k_empty[st]));
+        for (int t = 0; t < 2; ++t)
+          if (ok && j < nkv[t]) ok = is_qk ? issue_qk(t, j) : issue_pv(t, j);
+        // Frees the K (V) stage once the MMAs reading it have completed.
+        if (ok) ptx::tc_commit(ptx::smem_u32(&empty[st]));
         trace(1, 100 + j);
-        if (j > 0 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
-        }
       }
-      if (ok) ok = issue_pv(n_kv - 1);
       trace(1, ok ? 5 : 6);
       if (!ok) {
         set_abort(sm);
         // Drain: wait until every MMA this thread issued has completed.
-        ptx::tc_commit(ptx::smem_u32(&sm.drain));
-        ptx::mbar_wait_drain(ptx::smem_u32(&sm.drain), 0);
+        const uint32_t dr = ptx::smem_u32(&sm.drain[is_qk ? 0 : 1]);
+        ptx::tc_commit(dr);
+        ptx::mbar_wait_drain(dr, 0);
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warps 0-15
-    const int t = warp >> 3;                          // query tile
-    const int blk = 32 * (warp & 3) + 16 * ((warp >> 2) & 1);  // first row of this warp
-    const int qd = lane & 3;                          // column pair within each 8 columns
-    const int r0 = blk + (lane >> 2), r1 = r0 + 8;    // the two rows of this thread
+    // ------------------------------------------------------------ softmax warps 3-10
+    const int t = (warp - kFirstSoftmaxWarp) >> 2;  // query tile
+    const int row = 32 * (warp & 3) + lane;       // TMEM lane == row within the tile
     const int n = t ? nkv[1] : nkv[0];
     const int rows = t ? qrows[1] : qrows[0];
-    const uint32_t lane_base = tmem + ((uint32_t)blk << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const uint32_t cS = kColS0 + 128 * t, cP = kColP0 + 64 * t, cO = kColO0 + 64 * t;
-    const int64_t g0 = q0 + t * kBM + r0, g1 = g0 + 8;  // global query rows
+    const int64_t grow = q0 + t * kBM + row;  // global query row
     const uint32_t bar_s_full = ptx::smem_u32(&sm.s_full[t]);
     const uint32_t bar_s_free = ptx::smem_u32(&sm.s_free[t]);
     const uint32_t bar_p_full = ptx::smem_u32(&sm.p_full[t]);
     const uint32_t bar_o_done = ptx::smem_u32(&sm.o_done[t]);
-    const bool arrive_lane = lane < 16;  // 16 arrivals per warp x 8 warps = 128
     const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
-    float m0 = -INFINITY, m1 = -INFINITY;  // running offsets of rows r0, r1
-    float l0 = 0.f, l1 = 0.f;              // this thread's share of the row sums
+    float m = -INFINITY;  // running offset of this row (log2 units)
+    float l = 0.f;        // running sum of 2^(x - m)
     bool ok = n > 0;
     for (int j = 0; j < n; ++j) {
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_s_full, (uint32_t)j & 1, p.status));
       if (!ok) break;
       ptx::tc_fence_after();
-      uint32_t sr[64];
-      ptx::tmem_ld_16x256b_x16(lane_base + cS, sr);
+      uint32_t sr[128];
+      ptx::tmem_ld_32x32b_x64(lane_base + cS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
+      ptx::tmem_ld_32x32b_x64(lane_base + cS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
       ptx::tmem_wait_ld();
       ptx::tc_fence_before();
-      if (arrive_lane) ptx::mbar_arrive(bar_s_free);
-      if (t == 0 && warp == 0 && lane == 0) TL(4, j);
+      ptx::mbar_arrive(bar_s_free);
+      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(4 + 4 * t, j);
 
       const int64_t n0 = (int64_t)j * kBN;
       const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q0 + t * kBM + off);
       if (masked) {
-        const int64_t lim0 = (p.causal ? imin64(g0 + off, p.Sk - 1) : p.Sk - 1) - n0 - 2 * qd;
-        const int64_t lim1 = (p.causal ? imin64(g1 + off, p.Sk - 1) : p.Sk - 1) - n0 - 2 * qd;
+        const int64_t lim = (p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1) - n0;
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
+        for (int c = 0; c < 128; ++c)
+          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (8 * k + (e & 1) > ((e & 2) ? lim1 : lim0))
-              sr[4 * k + e] = __float_as_uint(-INFINITY);
+      for (int c = 0; c < 128; c += 8) {
+        a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        a3 = ptx::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
       }
-      float a0 = -INFINITY, a1 = -INFINITY, b0 = -INFINITY, b1 = -INFINITY;
-#pragma unroll
-      for (int k = 0; k < 16; k += 2) {
-        a0 = ptx::fmax3(a0, __uint_as_float(sr[4 * k]), __uint_as_float(sr[4 * k + 1]));
-        b0 = ptx::fmax3(b0, __uint_as_float(sr[4 * k + 2]), __uint_as_float(sr[4 * k + 3]));
-        a1 = ptx::fmax3(a1, __uint_as_float(sr[4 * k + 4]), __uint_as_float(sr[4 * k + 5]));
-        b1 = ptx::fmax3(b1, __uint_as_float(sr[4 * k + 6]), __uint_as_float(sr[4 * k + 7]));
+      const float mx = fmaxf(ptx::fmax3(a0, a1, a2), a3) * p.scale_log2;
+      float alpha = 1.f;
+      if (mx > m + kRescaleLog2) {  // first tile: m = -inf
+        alpha = ptx::ex2_approx(m - mx);
+        m = mx;
       }
-      const float mx0 = quad_max(fmaxf(a0, a1)) * p.scale_log2;
-      const float mx1 = quad_max(fmaxf(b0, b1)) * p.scale_log2;
-      float alpha0 = 1.f, alpha1 = 1.f;
-      if (mx0 > m0 + kRescaleLog2) {  // first tile: m = -inf
-        alpha0 = ptx::ex2_approx(m0 - mx0);
-        m0 = mx0;
-      }
-      if (mx1 > m1 + kRescaleLog2) {
-        alpha1 = ptx::ex2_approx(m1 - mx1);
-        m1 = mx1;
-      }
-      const uint64_t nm0 = ptx::f2_pack(-m0, -m0), nm1 = ptx::f2_pack(-m1, -m1);
+      const uint64_t nm = ptx::f2_pack(-m, -m);
       uint64_t s0 = 0, s1 = 0;  // bit pattern 0 == (0.f, 0.f)
-      uint32_t pk[32];
-      if (masked) {
+      // P row packed in place: pair c reads sr[2c], sr[2c+1] and writes sr[c],
+      // which pair c/2 has already read.
+      uint32_t(&pk)[64] = *reinterpret_cast<uint32_t(*)[64]>(&sr[0]);
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-#pragma unroll
-          for (int v = 0; v < 2; ++v) {
-            const uint64_t x2 = ptx::f2_fma(
-                ptx::f2_pack(__uint_as_float(sr[4 * k + 2 * v]), __uint_as_float(sr[4 * k + 2 * v + 1])),
-                c2, v ? nm1 : nm0);
-            const uint64_t p2 = exp2_mufu2(x2);
-            if (v)
-              s1 = ptx::f2_add(s1, p2);
-            else
-              s0 = ptx::f2_add(s0, p2);
-            float p0, p1;
-            ptx::f2_unpack(p2, p0, p1);
-            pk[2 * k + v] = ptx::pack_bf16x2(p0, p1);
-          }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-#pragma unroll
-          for (int v = 0; v < 2; ++v) {
-            const uint64_t x2 = ptx::f2_fma(
-                ptx::f2_pack(__uint_as_float(sr[4 * k + 2 * v]), __uint_as_float(sr[4 * k + 2 * v + 1])),
-                c2, v ? nm1 : nm0);
-            const bool poly = ((2 * k + v) & 7) < kPolyPairsOf8;
-            const uint64_t p2 = poly ? exp2_poly2(x2) : exp2_mufu2(x2);
-            if (v)
-              s1 = ptx::f2_add(s1, p2);
-            else
-              s0 = ptx::f2_add(s0, p2);
-            float p0, p1;
-            ptx::f2_unpack(p2, p0, p1);
-            pk[2 * k + v] = ptx::pack_bf16x2(p0, p1);
-          }
+      for (int c = 0; c < 64; ++c) {
+        const uint64_t x2 = ptx::f2_fma(
+            ptx::f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), c2, nm);
+        const bool poly = (c & 7) < kPolyPairsOf8;
+        const uint64_t p2 = poly ? exp2_poly2(x2) : exp2_mufu2(x2);
+        if (c & 1)
+          s1 = ptx::f2_add(s1, p2);
+        else
+          s0 = ptx::f2_add(s0, p2);
+        float p0, p1;
+        ptx::f2_unpack(p2, p0, p1);
+        pk[c] = ptx::pack_bf16x2(p0, p1);
       }
-      float x0, x1, y0, y1;
-      ptx::f2_unpack(s0, x0, x1);
-      ptx::f2_unpack(s1, y0, y1);
-      l0 = l0 * alpha0 + (x0 + x1);
-      l1 = l1 * alpha1 + (y0 + y1);
-      if (t == 0 && warp == 0 && lane == 0) TL(6, j);
+      {
+        float x0, x1;
+        ptx::f2_unpack(ptx::f2_add(s0, s1), x0, x1);
+        l = l * alpha + (x0 + x1);
+      }
 
       // P_j overwrites P_{j-1}: wait until P_{j-1}.V has completed (which also
-      // makes O final for the rescale).  P is stored first so its registers
-      // are free before O is loaded.
+      // makes O final for the rescale).
       if (j > 0) {
         ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(j - 1) & 1, p.status));
         if (!ok) break;
         ptx::tc_fence_after();
       }
-      ptx::tmem_st_16x128b_x16(lane_base + cP, pk);
-      if (j > 0 && __any_sync(0xffffffffu, alpha0 != 1.f || alpha1 != 1.f)) {
-        uint32_t o[32];
-        ptx::tmem_ld_16x256b_x8(lane_base + cO, o);
+      ptx::tmem_st_32x32b_x64(lane_base + cP, pk);
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        uint32_t o[64];
+        ptx::tmem_ld_32x32b_x64(lane_base + cO, o);
         ptx::tmem_wait_ld();
-        const uint64_t a20 = ptx::f2_pack(alpha0, alpha0), a21 = ptx::f2_pack(alpha1, alpha1);
+        const uint64_t a2 = ptx::f2_pack(alpha, alpha);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-#pragma unroll
-          for (int v = 0; v < 2; ++v) {
-            const uint64_t w2 = ptx::f2_mul(
-                ptx::f2_pack(__uint_as_float(o[4 * k + 2 * v]), __uint_as_float(o[4 * k + 2 * v + 1])),
-                v ? a21 : a20);
-            float w0, w1;
-            ptx::f2_unpack(w2, w0, w1);
-            o[4 * k + 2 * v] = __float_as_uint(w0);
-            o[4 * k + 2 * v + 1] = __float_as_uint(w1);
-          }
-        ptx::tmem_st_16x256b_x8(lane_base + cO, o);
+        for (int c = 0; c < 64; c += 2) {
+          float w0, w1;
+          ptx::f2_unpack(
+              ptx::f2_mul(ptx::f2_pack(__uint_as_float(o[c]), __uint_as_float(o[c + 1])), a2),
+              w0, w1);
+          o[c] = __float_as_uint(w0);
+          o[c + 1] = __float_as_uint(w1);
+        }
+        ptx::tmem_st_32x32b_x64(lane_base + cO, o);
       }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      if (arrive_lane) ptx::mbar_arrive(bar_p_full);
-      if (t == 0 && warp == 0 && lane == 0) TL(8, j);
-      if (warp == 8 * t && lane == 0) trace(3 + t, 100 + j);
+      ptx::mbar_arrive(bar_p_full);
+      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(12 + 4 * t, j);
+      if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, 100 + j);
     }
     if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(n - 1) & 1, p.status));
     if (ok) {
       ptx::tc_fence_after();
-      const float inv0 = 1.f / quad_sum(l0), inv1 = 1.f / quad_sum(l1);
-      uint32_t o[32];
-      ptx::tmem_ld_16x256b_x8(lane_base + cO, o);
+      const float inv = 1.f / l;
+      uint32_t o[64];
+      ptx::tmem_ld_32x32b_x64(lane_base + cO, o);
       ptx::tmem_wait_ld();
-      char *base = p.o + 2 * (b * p.os_b + h * p.os_h) + 4 * qd;
-      if (r0 < rows) {
-        char *dst = base + 2 * g0 * p.os_s;
+      if (row < rows) {
+        char *dst = p.o + 2 * (b * p.os_b + h * p.os_h + grow * p.os_s);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<uint32_t *>(dst + 16 * k) = ptx::pack_bf16x2(
-              __uint_as_float(o[4 * k]) * inv0, __uint_as_float(o[4 * k + 1]) * inv0);
-      }
-      if (r1 < rows) {
-        char *dst = base + 2 * g1 * p.os_s;
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<uint32_t *>(dst + 16 * k) = ptx::pack_bf16x2(
-              __uint_as_float(o[4 * k + 2]) * inv1, __uint_as_float(o[4 * k + 3]) * inv1);
+        for (int c = 0; c < 8; ++c) {
+          uint4 w;
+          const uint32_t *src = &o[8 * c];
+          w.x = ptx::pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+          w.y = ptx::pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+          w.z = ptx::pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+          w.w = ptx::pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+          reinterpret_cast<uint4 *>(dst)[c] = w;
+        }
       }
     } else if (n > 0) {
       set_abort(sm);
     }
-    if (warp == 8 * t && lane == 0) trace(3 + t, ok ? 5 : 6);
+    if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, ok ? 5 : 6);
   }
 
   ptx::tc_fence_before();
@@ -528,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = threadIdx.x; i < 24 * 64; i += kThreads)
       reinterpret_cast<volatile unsigned long long *>(g_trace + 4096)[i] = (&sm.tl[0][0])[i];
 #endif
-  if (warp == kMmaWarp) {
+  if (warp == kMmaQkWarp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
     if (lane == 0) trace(1, 8);

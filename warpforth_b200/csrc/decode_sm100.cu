@@ -2,19 +2,25 @@
 // over a padded bf16 KV cache, split over 256-key chunks (split-KV).
 //
 // The step is HBM-bound: every valid K and V byte is read exactly once and
-// nothing else of size is touched.  Per CTA (one (batch, head, chunk)):
-//   1. one thread issues two bulk copies (cp.async.bulk, async proxy) of
-//      exactly the chunk's valid K rows and V rows into shared memory -- the
-//      padding past kv_lens[b] is never read;
-//   2. scores: 8 lanes per key, 16-byte smem loads, 3-step xor-shuffle dot
-//      reduction; the query is pre-scaled by scale*log2(e);
-//   3. chunk max / sum with warp shuffles, p = exp2(s - m);
-//   4. P.V: 8 lanes x 8 columns per key row, 4 rows per warp step, shuffle +
-//      smem reduction over key groups and warps;
-//   5. the partial (m, l, acc[64]) of the chunk goes to the workspace.
+// nothing else of size is touched.  A persistent grid (one CTA per SM) walks
+// the (chunk, batch, head) work items round-robin -- chunk-major, so every
+// CTA gets the same mix of early and late chunks -- and skips chunks past
+// kv_lens[b] without touching memory.  Warp roles, all decoupled through
+// mbarriers (no CTA-wide barrier once the loop runs):
+//   * producer (warp 8): keeps kStages chunks in flight; for each item it
+//     issues bulk copies (cp.async.bulk) of the query row and of exactly the
+//     chunk's valid K rows and V rows into a free stage -- the cache padding
+//     is never read;
+//   * consumers (warps 0-7): warp w takes keys [32w, 32w+32) of the chunk and
+//     runs the whole softmax on them in registers: 8 lanes per key (16-byte
+//     smem loads, xor-shuffle dot reduction, query pre-scaled by
+//     scale*log2(e)), warp max / sum by shuffles, p = exp2(s - m_warp), then
+//     P.V with the same lanes (8 columns each); it frees the stage and hands
+//     its (m, l, acc[64]) to the merge warp;
+//   * merge (warp 9): folds the 8 warp partials of a chunk into the chunk's
+//     partial in the workspace.
 // A second kernel merges the partials of each (batch, head) (one warp each)
-// and writes the f32 output.  K/V loads for the score phase overlap the V
-// transfer (separate barriers), and ~3 CTAs per SM keep loads in flight.
+// and writes the f32 output.
 #include <math.h>
 
 #include <mutex>
@@ -26,23 +32,38 @@
 namespace wfattn {
 namespace {
 
-constexpr int kChunk = 256;  // keys per CTA
+constexpr int kChunk = 256;  // keys per work item
 constexpr int kD = 64;
-constexpr int kThreads = 128;
+constexpr int kStages = 3;
+constexpr int kConsumerWarps = 8;
+constexpr int kKeysPerWarp = kChunk / kConsumerWarps;
+constexpr int kSteps = kKeysPerWarp / 4;  // 4 keys per warp step (8 lanes each)
+constexpr int kProducerWarp = kConsumerWarps, kMergeWarp = kConsumerWarps + 1;
+constexpr int kThreads = 32 * (kConsumerWarps + 2);
 constexpr uint32_t kRowBytes = kD * 2;
+constexpr uint32_t kStageBytes = kChunk * kRowBytes;
 constexpr int kPartFloats = kD + 2;  // acc[64], m, l
+constexpr int kMergeStride = kD + 4;  // a warp's row in smem: acc[64], m, l, pad to 16 B
+
+struct ItemInfo {
+  int64_t bh;
+  int c, n;  // chunk index, valid keys (-1: no more work)
+};
 
 struct DecSmem {
-  uint8_t k[kChunk * kRowBytes];
-  uint8_t v[kChunk * kRowBytes];
-  float s[kChunk];
-  float oacc[4][kD];
-  float red[8];
-  uint64_t bar_k, bar_v;
+  uint8_t k[kStages][kStageBytes];
+  uint8_t v[kStages][kStageBytes];
+  uint8_t q[kStages][kRowBytes];
+  float merge[kStages][kConsumerWarps][kMergeStride];  // warp partials of a use of a stage
+  ItemInfo item[kStages];        // written by the producer, read by the consumers
+  ItemInfo merge_item[kStages];  // copy for the merge warp (item[] is refilled earlier)
+  uint64_t full[kStages], empty[kStages];       // producer <-> consumers
+  uint64_t merged[kStages], merge_free[kStages];  // consumers <-> merge warp
+  uint32_t abort;
 };
 
 struct DecParams {
-  int64_t H, max_len;
+  int64_t B, H, max_len;
   int nch;  // chunks per (batch, head) = ceil(max_len / kChunk)
   const char *q, *k, *v;
   int64_t qs_b, qs_h, ks_b, ks_h, vs_b, vs_h;  // element strides (seq stride is kD)
@@ -69,123 +90,231 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 &w, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecParams p) {
+__global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecParams p) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   DecSmem &sm = *reinterpret_cast<DecSmem *>(dsm_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (ptx::timeout_flagged(p.status)) return;  // sticky until the host clears it
-  const int64_t bh = blockIdx.x / p.nch;
-  const int c = blockIdx.x % p.nch;
-  const int64_t b = bh / p.H, h = bh % p.H;
-  const int64_t L = clamp_len(p.kv_lens[b], p.max_len, threadIdx.x == 0 ? p.status : nullptr);
-  const int64_t t0 = (int64_t)c * kChunk;
-  if (t0 >= L) return;  // no valid keys in this chunk; the combine skips it
-  const int n = (int)imin64(kChunk, L - t0);
+  volatile uint32_t &abort_flag = sm.abort;
 
-  const uint32_t bar_k = ptx::smem_u32(&sm.bar_k), bar_v = ptx::smem_u32(&sm.bar_v);
   if (threadIdx.x == 0) {
-    ptx::mbar_init(bar_k, 1);
-    ptx::mbar_init(bar_v, 1);
+    for (int i = 0; i < kStages; ++i) {
+      ptx::mbar_init(ptx::smem_u32(&sm.full[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sm.empty[i]), kConsumerWarps);
+      ptx::mbar_init(ptx::smem_u32(&sm.merged[i]), kConsumerWarps);
+      ptx::mbar_init(ptx::smem_u32(&sm.merge_free[i]), 1);
+    }
+    abort_flag = 0;
     ptx::fence_barrier_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t bytes = (uint32_t)n * kRowBytes;
-    const char *ksrc = p.k + 2 * (b * p.ks_b + h * p.ks_h + t0 * kD);
-    const char *vsrc = p.v + 2 * (b * p.vs_b + h * p.vs_h + t0 * kD);
-    ptx::mbar_arrive_expect_tx(bar_k, bytes);
-    ptx::bulk_load(ptx::smem_u32(sm.k), ksrc, bytes, bar_k);
-    ptx::mbar_arrive_expect_tx(bar_v, bytes);
-    ptx::bulk_load(ptx::smem_u32(sm.v), vsrc, bytes, bar_v);
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int64_t BH = p.B * p.H, total = BH * p.nch;
+      int uses = 0;  // stage uses so far (items with data)
+      bool ok = true;
+      for (int64_t it = blockIdx.x; ok && it < total; it += gridDim.x) {
+        const int c = (int)(it / BH);
+        const int64_t bh = it % BH;
+        const int64_t b = bh / p.H, h = bh % p.H;
+        const int64_t L = clamp_len(p.kv_lens[b], p.max_len, p.status);
+        const int64_t t0 = (int64_t)c * kChunk;
+        if (t0 >= L) continue;  // no valid keys; the combine skips this chunk
+        const int n = (int)imin64(kChunk, L - t0);
+        const int st = uses % kStages;
+        if (uses >= kStages &&
+            !ptx::mbar_wait(ptx::smem_u32(&sm.empty[st]), (uint32_t)(uses / kStages - 1) & 1,
+                            p.status)) {
+          ok = false;
+          break;
+        }
+        if (abort_flag) {
+          ok = false;
+          break;
+        }
+        sm.item[st].bh = bh;
+        sm.item[st].c = c;
+        sm.item[st].n = n;
+        const uint32_t bytes = (uint32_t)n * kRowBytes;
+        const char *qsrc = p.q + 2 * (b * p.qs_b + h * p.qs_h);
+        const char *ksrc = p.k + 2 * (b * p.ks_b + h * p.ks_h + t0 * kD);
+        const char *vsrc = p.v + 2 * (b * p.vs_b + h * p.vs_h + t0 * kD);
+        const uint32_t fb = ptx::smem_u32(&sm.full[st]);
+        ptx::mbar_arrive_expect_tx(fb, 2 * bytes + kRowBytes);
+        ptx::bulk_load(ptx::smem_u32(sm.q[st]), qsrc, kRowBytes, fb);
+        ptx::bulk_load(ptx::smem_u32(sm.k[st]), ksrc, bytes, fb);
+        ptx::bulk_load(ptx::smem_u32(sm.v[st]), vsrc, bytes, fb);
+        ++uses;
+      }
+      if (ok) {
+        // End marker: a stage whose item has n = -1, published without data.
+        const int st = uses % kStages;
+        ok = uses < kStages ||
+             ptx::mbar_wait(ptx::smem_u32(&sm.empty[st]), (uint32_t)(uses / kStages - 1) & 1,
+                            p.status);
+        if (ok) {
+          sm.item[st].n = -1;
+          ptx::mbar_arrive(ptx::smem_u32(&sm.full[st]));
+        }
+      }
+      if (!ok) {
+        abort_flag = 1;
+        // Drain: every copy this thread issued must land before the CTA exits.
+        for (int i = uses < kStages ? uses : kStages; i > 0; --i) {
+          const int u = uses - i;
+          ptx::mbar_wait_drain(ptx::smem_u32(&sm.full[u % kStages]), (uint32_t)(u / kStages) & 1);
+        }
+      }
+    }
+    return;
   }
 
-  // Query slice of this lane group: columns [8g, 8g+8), pre-scaled.
-  const int g = lane & 7, sub = lane >> 3;
-  float qf[8];
-  {
-    const uint4 w = *reinterpret_cast<const uint4 *>(p.q + 2 * (b * p.qs_b + h * p.qs_h) + g * 16);
-    bf16x8_to_f32(w, qf);
+  if (warp == kMergeWarp) {
+    // ------------------------------------------------------------ merge warp
+    // Lane l folds columns 2l, 2l+1; lane 0 also the row max and sum.
+    for (int u = 0;; ++u) {
+      const int st = u % kStages;
+      const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(ptx::smem_u32(&sm.merged[st]),
+                                                             (uint32_t)(u / kStages) & 1, p.status));
+      if (!ok) {
+        abort_flag = 1;
+        break;
+      }
+      const ItemInfo item = sm.merge_item[st];
+      if (item.n < 0) break;
+      const float(*mw)[kMergeStride] = sm.merge[st];
+      float M = mw[0][kD];
+#pragma unroll
+      for (int w = 1; w < kConsumerWarps; ++w) M = fmaxf(M, mw[w][kD]);
+      float a0 = 0.f, a1 = 0.f, l = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        // warp 0 always has keys, so M is finite and 2^(-inf - M) = 0
+        const float s = ptx::ex2_approx(mw[w][kD] - M);
+        const float2 a = *reinterpret_cast<const float2 *>(&mw[w][2 * lane]);
+        a0 = fmaf(a.x, s, a0);
+        a1 = fmaf(a.y, s, a1);
+        l = fmaf(mw[w][kD + 1], s, l);
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&sm.merge_free[st]));
+      float *part = p.part + ((size_t)item.bh * p.nch + item.c) * kPartFloats;
+      *reinterpret_cast<float2 *>(part + 2 * lane) = make_float2(a0, a1);
+      if (lane == 0) {
+        part[kD] = M;
+        part[kD + 1] = l;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g = lane & 7, sub = lane >> 3;  // column group, key within a step
+  for (int u = 0;; ++u) {
+    const int st = u % kStages;
+    const uint32_t par = (uint32_t)(u / kStages) & 1;
+    bool ok = __all_sync(0xffffffffu,
+                         ptx::mbar_wait(ptx::smem_u32(&sm.full[st]), par, p.status));
+    // The merge slot of this stage is free again once its previous use is merged.
+    if (ok && u >= kStages)
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(ptx::smem_u32(&sm.merge_free[st]), par ^ 1,
+                                                  p.status));
+    if (!ok) {
+      abort_flag = 1;
+      break;
+    }
+    const ItemInfo item = sm.item[st];
+    if (item.n < 0) {
+      // Tell the merge warp there is no more work, then stop.
+      if (lane == 0) {
+        if (warp == 0) sm.merge_item[st].n = -1;
+        ptx::mbar_arrive(ptx::smem_u32(&sm.merged[st]));
+      }
+      break;
+    }
+    const int n = item.n;
+
+    // Query slice of this lane: columns [8g, 8g+8), pre-scaled.
+    float qf[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4 *>(sm.q[st] + g * 16), qf);
 #pragma unroll
     for (int i = 0; i < 8; ++i) qf[i] *= p.scale_log2;
-  }
 
-  // CTA-uniform outcome: every thread takes the same path through the
-  // barriers and full-warp shuffles below.
-  bool ok = __syncthreads_and(ptx::mbar_wait(bar_k, 0, p.status)) != 0;
-  // ---- scores: keys t = 4*warp + sub + 16*i.  The loop bound depends on the
-  // warp only, so all 32 lanes run the same iterations and reach every
-  // full-mask shuffle together; lanes past the end of the chunk just idle.
-  for (int base = warp * 4; ok && base < n; base += 16) {
-    const int t = base + sub;
-    float d = 0.f;
-    if (t < n) {
-      const uint4 w = *reinterpret_cast<const uint4 *>(sm.k + t * kRowBytes + g * 16);
-      float kf[8];
-      bf16x8_to_f32(w, kf);
+    // ---- scores of this warp's keys t_i = kKeysPerWarp*warp + 4*i + sub (all
+    // 8 lanes of a key group end up holding its score).
+    const int t_base = kKeysPerWarp * warp + sub;
+    const uint8_t *ks = sm.k[st] + g * 16;
+    float sc[kSteps];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) d = fmaf(qf[i], kf[i], d);
+    for (int i = 0; i < kSteps; ++i) {
+      const int t = t_base + 4 * i;
+      float d = 0.f;
+      if (t < n) {
+        float kf[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(ks + t * kRowBytes), kf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d = fmaf(qf[e], kf[e], d);
+      }
+      sc[i] = d;
     }
-    d += __shfl_xor_sync(0xffffffffu, d, 1);
-    d += __shfl_xor_sync(0xffffffffu, d, 2);
-    d += __shfl_xor_sync(0xffffffffu, d, 4);
-    if (g == 0 && t < n) sm.s[t] = d;
-  }
-  __syncthreads();
-
-  // ---- chunk max and exp2
-  float mx = -INFINITY;
-  for (int t = threadIdx.x; t < n; t += kThreads) mx = fmaxf(mx, sm.s[t]);
 #pragma unroll
-  for (int sh = 16; sh > 0; sh >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, sh));
-  if (lane == 0) sm.red[warp] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(sm.red[0], sm.red[1]), fmaxf(sm.red[2], sm.red[3]));
-  float sum = 0.f;
-  for (int t = threadIdx.x; t < n; t += kThreads) {
-    const float e = ptx::ex2_approx(sm.s[t] - mx);
-    sm.s[t] = e;
-    sum += e;
-  }
+    for (int i = 0; i < kSteps; ++i) {
+      sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 1);
+      sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 2);
+      sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 4);
+    }
+    // ---- warp softmax over its keys
+    float m = -INFINITY;
 #pragma unroll
-  for (int sh = 16; sh > 0; sh >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, sh);
-  if (lane == 0) sm.red[4 + warp] = sum;
-  __syncthreads();
-
-  // ---- P.V
-  ok = __syncthreads_and(ok && ptx::mbar_wait(bar_v, 0, p.status)) != 0;
-  float acc[8];
+    for (int i = 0; i < kSteps; ++i)
+      if (t_base + 4 * i < n) m = fmaxf(m, sc[i]);
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+    float l = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  for (int t = warp * 4 + sub; ok && t < n; t += 16) {
-    const float pt = sm.s[t];
-    const uint4 w = *reinterpret_cast<const uint4 *>(sm.v + t * kRowBytes + g * 16);
-    float vf[8];
-    bf16x8_to_f32(w, vf);
+    for (int i = 0; i < kSteps; ++i) {
+      sc[i] = t_base + 4 * i < n ? ptx::ex2_approx(sc[i] - m) : 0.f;
+      l += sc[i];
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+    // ---- P.V over the same keys; lane holds columns [8g, 8g+8)
+    const uint8_t *vs = sm.v[st] + g * 16;
+    float acc[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = fmaf(pt, vf[i], acc[i]);
-  }
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 8);
-    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
-  }
-  if (sub == 0) {
+    for (int i = 0; i < kSteps; ++i) {
+      const int t = t_base + 4 * i;
+      if (t < n) {
+        float vf[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(vs + t * kRowBytes), vf);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sm.oacc[warp][g * 8 + i] = acc[i];
-  }
-  __syncthreads();
-  float *part = p.part + ((size_t)bh * p.nch + c) * kPartFloats;
-  if (threadIdx.x < kD) {
-    const int d = threadIdx.x;
-    part[d] = sm.oacc[0][d] + sm.oacc[1][d] + sm.oacc[2][d] + sm.oacc[3][d];
-  } else if (threadIdx.x == kD) {
-    part[kD] = ok ? mx : -INFINITY;
-    part[kD + 1] = ok ? (sm.red[4] + sm.red[5] + sm.red[6] + sm.red[7]) : 0.f;
-  }
-  if (!ok && threadIdx.x == 0) {
-    // Drain: both bulk copies must land before the CTA releases its shared memory.
-    ptx::mbar_wait_drain(bar_k, 0);
-    ptx::mbar_wait_drain(bar_v, 0);
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(sc[i], vf[e], acc[e]);
+      }
+    }
+    // The stage's K, V and query are no longer read by this warp.
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&sm.empty[st]));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 8);
+      acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 16);
+    }
+    float *mw = sm.merge[st][warp];
+    if (sub == 0) {
+      *reinterpret_cast<float4 *>(&mw[8 * g]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4 *>(&mw[8 * g + 4]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+    if (lane == 0) {
+      mw[kD] = m;  // -inf for a warp without keys (then l = 0, acc = 0)
+      mw[kD + 1] = l;
+      if (warp == 0) sm.merge_item[st] = item;
+    }
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&sm.merged[st]));
   }
 }
 
@@ -265,6 +394,7 @@ size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t) {
 cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
   if (a.ks.s != kD || a.vs.s != kD) return cudaErrorInvalidValue;  // rows must be contiguous
   DecParams p;
+  p.B = a.B;
   p.H = a.H;
   p.max_len = a.max_len;
   p.nch = (int)((a.max_len + kChunk - 1) / kChunk);
@@ -281,8 +411,8 @@ cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaS
   p.part = static_cast<float *>(a.workspace);
   p.scale_log2 = (float)((double)a.scale * 1.4426950408889634);
   p.status = dev.status;
-  const int64_t blocks = a.B * a.H * p.nch;
-  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const int64_t items = a.B * a.H * p.nch;
+  const int64_t blocks = items < dev.sm_count ? items : dev.sm_count;
   const size_t smem = sizeof(DecSmem);
   cudaError_t err = cudaFuncSetAttribute(decode_split_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -60,6 +60,19 @@ def test_decode_ragged_lengths(wf, lens):
     assert _rel(out, _ref(q, kc, vc, kl)) <= BF16_REL_TOL
 
 
+def test_decode_many_batches_unplanned_order(wf):
+    # more batches than the kernel orders by length in shared memory (1024):
+    # the work items are then enumerated chunk-major with empty chunks skipped
+    b = 1100
+    lens = torch.randint(1, 301, (b,), generator=torch.Generator().manual_seed(15),
+                         dtype=torch.int32).tolist()
+    q, kc, vc, kl = _case(b, 1, 300, lens, 14)
+    out = wf.decode(q.cuda(), kc.cuda(), vc.cuda(), kl.cuda()).cpu().numpy()
+    assert np.isfinite(out).all()
+    sel = list(range(0, 40)) + list(range(b - 40, b))
+    assert _rel(out[sel], _ref(q[sel], kc[sel], vc[sel], kl[sel])) <= BF16_REL_TOL
+
+
 def test_decode_padding_is_never_read(wf):
     # NaN in the padding past kv_lens must not reach the output
     q, kc, vc, kl = _case(2, 2, 600, [300, 512], 12)

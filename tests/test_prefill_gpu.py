@@ -142,6 +142,31 @@ def test_bf16_sizes(wf, s):
     assert _bf16_rel_err(out, _oracle(q, k, v)) <= BF16_REL_TOL
 
 
+# The library runs the one-tile kernel when ceil(Sq/256)*B*H is below the SM
+# count (148 on B200) and the two-tile kernel otherwise: the small cases above
+# take the first, the B*H = 160 cases below the second.
+@pytest.mark.parametrize("s", [1, 129, 256, 300, 1000])
+def test_bf16_two_tile_kernel_sizes(wf, s):
+    q, k, v = (_randn((2, 80, s, 64), 450 + i, torch.bfloat16) for i in range(3))
+    out = wf.attention(q.cuda(), k.cuda(), v.cuda()).float().cpu().numpy()
+    assert np.isfinite(out).all()
+    flat = (1, 160, s, 64)
+    for lo, hi in ((0, 3), (157, 160)):
+        ref = _oracle(q, k, v, bh_range=(lo, hi)).reshape(flat)
+        assert _bf16_rel_err(out.reshape(flat)[:, lo:hi], ref[:, lo:hi]) <= BF16_REL_TOL
+
+
+def test_bf16_two_tile_kernel_noncausal_cross_lengths(wf):
+    qq = _randn((2, 80, 130, 64), 460, torch.bfloat16)
+    kk, vv = (_randn((2, 80, 333, 64), 461 + i, torch.bfloat16) for i in range(2))
+    flat_q = (1, 160, 130, 64)
+    for causal in (True, False):
+        out = wf.attention(qq.cuda(), kk.cuda(), vv.cuda(), causal=causal,
+                           scale=0.2).float().cpu().numpy().reshape(flat_q)
+        ref = _oracle(qq, kk, vv, causal=causal, scale=0.2, bh_range=(150, 160)).reshape(flat_q)
+        assert _bf16_rel_err(out[:, 150:], ref[:, 150:]) <= BF16_REL_TOL
+
+
 def test_bf16_strided_noncausal_cross_lengths(wf):
     base = _randn((2, 200, 3, 4, 64), 500, torch.bfloat16).cuda()
     q, k, v = (base[:, :, i].transpose(1, 2) for i in range(3))

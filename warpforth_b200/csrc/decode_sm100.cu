@@ -3,21 +3,21 @@
 //
 // The step is HBM-bound: every valid K and V byte is read exactly once and
 // nothing else of size is touched.  A persistent grid (one CTA per SM) walks
-// the (chunk, batch, head) work items round-robin -- chunk-major, so every
-// CTA gets the same mix of early and late chunks -- and skips chunks past
-// kv_lens[b] without touching memory.  Warp roles, all decoupled through
-// mbarriers (no CTA-wide barrier once the loop runs):
-//   * producer (warp 8): keeps kStages chunks in flight; for each item it
+// the (chunk, batch, head) work items that hold keys round-robin: chunk-major,
+// with the batches ordered by length, so the CTAs' loads differ by at most one
+// item (chunks past kv_lens[b] are never visited).  Warp roles, all decoupled
+// through mbarriers (no CTA-wide barrier once the loop runs):
+//   * producer (warp 16): keeps kStages chunks in flight; for each item it
 //     issues bulk copies (cp.async.bulk) of the query row and of exactly the
 //     chunk's valid K rows and V rows into a free stage -- the cache padding
 //     is never read;
-//   * consumers (warps 0-7): warp w takes keys [32w, 32w+32) of the chunk and
+//   * consumers (warps 0-15): warp w takes keys [16w, 16w+16) of the chunk and
 //     runs the whole softmax on them in registers: 8 lanes per key (16-byte
 //     smem loads, xor-shuffle dot reduction, query pre-scaled by
 //     scale*log2(e)), warp max / sum by shuffles, p = exp2(s - m_warp), then
 //     P.V with the same lanes (8 columns each); it frees the stage and hands
 //     its (m, l, acc[64]) to the merge warp;
-//   * merge (warp 9): folds the 8 warp partials of a chunk into the chunk's
+//   * merge (warp 17): folds the 16 warp partials of a chunk into the chunk's
 //     partial in the workspace.
 // A second kernel merges the partials of each (batch, head) (one warp each)
 // and writes the f32 output.
@@ -35,7 +35,7 @@ namespace {
 constexpr int kChunk = 256;  // keys per work item
 constexpr int kD = 64;
 constexpr int kStages = 3;
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kKeysPerWarp = kChunk / kConsumerWarps;
 constexpr int kSteps = kKeysPerWarp / 4;  // 4 keys per warp step (8 lanes each)
 constexpr int kProducerWarp = kConsumerWarps, kMergeWarp = kConsumerWarps + 1;
@@ -44,6 +44,7 @@ constexpr uint32_t kRowBytes = kD * 2;
 constexpr uint32_t kStageBytes = kChunk * kRowBytes;
 constexpr int kPartFloats = kD + 2;  // acc[64], m, l
 constexpr int kMergeStride = kD + 4;  // a warp's row in smem: acc[64], m, l, pad to 16 B
+constexpr int kPlanMaxB = 1024;  // batches the in-smem work plan can order
 
 struct ItemInfo {
   int64_t bh;
@@ -59,6 +60,10 @@ struct DecSmem {
   ItemInfo merge_item[kStages];  // copy for the merge warp (item[] is refilled earlier)
   uint64_t full[kStages], empty[kStages];       // producer <-> consumers
   uint64_t merged[kStages], merge_free[kStages];  // consumers <-> merge warp
+  // Work plan (batch <= kPlanMaxB): batches ordered by chunk count, descending.
+  int plan_nch[kPlanMaxB];  // chunks of batch b
+  int plan_b[kPlanMaxB];    // batch at each rank
+  int plan_len[kPlanMaxB];  // its (clamped) kv length
   uint32_t abort;
 };
 
@@ -107,21 +112,90 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecPara
     abort_flag = 0;
     ptx::fence_barrier_init();
   }
+  // Work plan.  The items with data are (chunk c, batch b, head h) with
+  // c < nch_b; enumerated chunk-major with the batches in descending nch_b
+  // order, those of chunk c form one contiguous run, so CTA i can take every
+  // gridDim-th item with data and the CTAs' loads differ by at most one item.
+  const bool planned = p.B <= kPlanMaxB;
+  if (planned) {
+    for (int b = threadIdx.x; b < p.B; b += kThreads) {
+      const int64_t L = clamp_len(p.kv_lens[b], p.max_len, p.status);
+      sm.plan_nch[b] = (int)((L + kChunk - 1) / kChunk);
+      sm.plan_len[b] = (int)L;
+    }
+    __syncthreads();
+    int rank_of[(kPlanMaxB + kThreads - 1) / kThreads];
+#pragma unroll
+    for (int i = 0; i < (kPlanMaxB + kThreads - 1) / kThreads; ++i) {
+      const int b = threadIdx.x + i * kThreads;
+      rank_of[i] = 0;
+      if (b < p.B) {
+        const int nb = sm.plan_nch[b];
+        for (int o = 0; o < p.B; ++o) {
+          const int no = sm.plan_nch[o];
+          rank_of[i] += (no > nb) || (no == nb && o < b);
+        }
+      }
+    }
+    int len_of[(kPlanMaxB + kThreads - 1) / kThreads];
+#pragma unroll
+    for (int i = 0; i < (kPlanMaxB + kThreads - 1) / kThreads; ++i) {
+      const int b = threadIdx.x + i * kThreads;
+      len_of[i] = b < p.B ? sm.plan_len[b] : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < (kPlanMaxB + kThreads - 1) / kThreads; ++i) {
+      const int b = threadIdx.x + i * kThreads;
+      if (b < p.B) {
+        sm.plan_b[rank_of[i]] = b;
+        sm.plan_len[rank_of[i]] = len_of[i];
+      }
+    }
+  }
   __syncthreads();
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int64_t BH = p.B * p.H, total = BH * p.nch;
+      const int64_t BH = p.B * p.H;
+      // Planned: items with data only.  Otherwise: every (c, b, h), skipping
+      // the chunks past kv_lens[b].
+      int64_t total = BH * p.nch;
+      if (planned) {
+        total = 0;
+        for (int r = 0; r < p.B; ++r) total += (int64_t)p.H * sm.plan_nch[sm.plan_b[r]];
+      }
+      int c_run = 0, r_end = 0;  // planned walk: current chunk, batches with nch > c_run
+      int64_t run0 = 0;          // first item of chunk c_run
+      if (planned)
+        while (r_end < p.B && sm.plan_nch[sm.plan_b[r_end]] > 0) ++r_end;
       int uses = 0;  // stage uses so far (items with data)
       bool ok = true;
       for (int64_t it = blockIdx.x; ok && it < total; it += gridDim.x) {
-        const int c = (int)(it / BH);
-        const int64_t bh = it % BH;
-        const int64_t b = bh / p.H, h = bh % p.H;
-        const int64_t L = clamp_len(p.kv_lens[b], p.max_len, p.status);
+        int c;
+        int64_t b, h, L;
+        if (planned) {
+          while (it >= run0 + (int64_t)p.H * r_end) {  // next chunk index
+            run0 += (int64_t)p.H * r_end;
+            ++c_run;
+            while (r_end > 0 && sm.plan_nch[sm.plan_b[r_end - 1]] <= c_run) --r_end;
+          }
+          const int64_t j = it - run0;
+          const int r = (int)(j / p.H);
+          c = c_run;
+          b = sm.plan_b[r];
+          h = j % p.H;
+          L = sm.plan_len[r];
+        } else {
+          c = (int)(it / BH);
+          b = (it % BH) / p.H;
+          h = it % p.H;
+          L = clamp_len(p.kv_lens[b], p.max_len, p.status);
+          if ((int64_t)c * kChunk >= L) continue;  // no valid keys; the combine skips it
+        }
+        const int64_t bh = b * p.H + h;
         const int64_t t0 = (int64_t)c * kChunk;
-        if (t0 >= L) continue;  // no valid keys; the combine skips this chunk
         const int n = (int)imin64(kChunk, L - t0);
         const int st = uses % kStages;
         if (uses >= kStages &&
@@ -413,6 +487,7 @@ cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaS
   p.status = dev.status;
   const int64_t items = a.B * a.H * p.nch;
   const int64_t blocks = items < dev.sm_count ? items : dev.sm_count;
+  static_assert(sizeof(DecSmem) <= 227 * 1024, "shared memory budget");
   const size_t smem = sizeof(DecSmem);
   cudaError_t err = cudaFuncSetAttribute(decode_split_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -176,10 +176,13 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
       if ((ext_q[i] > 1 && sq[i] == 0) || (ext_k[i] > 1 && (sk[i] == 0 || sv[i] == 0)))
         return fail(WFATTN_INVALID_ARG, "bf16 path does not take zero (broadcast) strides");
     }
-    // The two-tile kernel is the default; WFATTN_PREFILL_1Q=1 selects the
-    // one-tile kernel (kept for comparison measurements).
-    static const bool one_tile = getenv("WFATTN_PREFILL_1Q") != nullptr;
-    err = one_tile ? launch_prefill_bf16_1q(a, dev, s) : launch_prefill_bf16_2q(a, dev, s);
+    // Two 128-row query tiles per CTA (one CTA per SM) halve the K/V traffic
+    // per FLOP; when that grid would not even give every SM a CTA, one tile
+    // per CTA (two CTAs per SM) spreads the few rows over twice the SMs and
+    // halves the longest CTA.
+    const int64_t two_tile_ctas = (a.Sq + 255) / 256 * a.B * a.H;
+    err = two_tile_ctas < dev.sm_count ? launch_prefill_bf16_1q(a, dev, s)
+                                       : launch_prefill_bf16_2q(a, dev, s);
     if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
     return WFATTN_OK;
   }

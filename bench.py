@@ -279,7 +279,7 @@ def config_of(w: Workload, n: int) -> dict:
     else:
         cfg.update({"max_kv_len": w.S, "kv_lens": "U[512,4096] seed 3 (sum 142652)",
                     "parallelism": f"replicas/{n}" if n > 1 else "single",
-                    "l2": "L2 flushed between timed steps (256 MB write)"})
+                    "l2": "inputs larger than L2 (913 MB of K/V read per step, 126 MB L2)"})
     return cfg
 
 
@@ -490,7 +490,10 @@ def run_gpu(args, w: Workload) -> None:
         return float(t.item())
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    needs_flush = not (w.kind == "prefill" and w.S >= 4096)
+    # A step whose inputs exceed L2 (126 MB) needs no flush: long prefill and
+    # decode (913 MB of K/V per step).  A flush by writes would also leave L2
+    # full of dirty lines whose write-back the next step would pay for.
+    needs_flush = w.kind == "prefill" and w.S < 4096
 
     # ---------------- inputs (identical on every rank) and the step
     tdt = torch.bfloat16 if w.dtype == "bf16" else torch.float32
@@ -627,7 +630,10 @@ def run_gpu(args, w: Workload) -> None:
             peak = float(peaks["hbm_gbs"])
             roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs"}
-        roof["traffic"] = load_traffic(w)
+        traffic = load_traffic(w)
+        if traffic is not None and w.sharded:
+            traffic = int(traffic * local_heads / w.H)  # this rank's launch
+        roof["traffic"] = traffic
         roof["kernel_ms"] = kernel_ms_max
         line = {
             "metric": metric, "value": value, "unit": unit, "n_gpus": world,

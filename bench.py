@@ -230,7 +230,7 @@ def run_reference(args, w: Workload) -> None:
         return
     import oracle
 
-    threads = oracle.max_threads()
+    threads = host_threads()
     metric, unit, hib = metric_of(w)
     vals = []
     sample = None
@@ -604,7 +604,7 @@ def run_gpu(args, w: Workload) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
 
-        threads = oracle.max_threads()
+        threads = host_threads()
         r = cpu_sample(w, args.cpu_seconds, threads)
         cpu = {"value": r["value"], "unit": r["unit"], "cores": threads, "kind": "port",
                "sample": r["sample"]}
@@ -736,6 +736,15 @@ def run_e2e(args, w, world, rank, dev, tdt, barrier, max_over_ranks, wf, sp, uni
             else "GB/s", "ms_per_step": ms, "steps": steps,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "path": "warpforth_b200.warpforth (ctypes) -> libwfattn C ABI, pinned host buffers"}
+
+
+def host_threads() -> int:
+    """Host cores this process may run on.  torchrun sets OMP_NUM_THREADS=1 for every rank, so
+    the CPU legs pass their thread count explicitly instead of taking OpenMP's default."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def load_traffic(w: Workload):

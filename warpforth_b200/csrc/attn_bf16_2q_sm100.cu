@@ -357,24 +357,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       ptx::tc_fence_after();
       uint32_t sr[128];
+      const int64_t n0 = (int64_t)j * kBN;
+      const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q0 + t * kBM + off);
+      const int64_t lim = masked ? (p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1) - n0 : 127;
+      float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
       ptx::tmem_ld_32x32b_x64(lane_base + cS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
+      ptx::tmem_wait_ld();
       ptx::tmem_ld_32x32b_x64(lane_base + cS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+      // the first half's max overlaps the second half's load
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+      }
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        a3 = ptx::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
       ptx::tmem_wait_ld();
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar_s_free);
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(4 + 4 * t, j);
-
-      const int64_t n0 = (int64_t)j * kBN;
-      const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q0 + t * kBM + off);
       if (masked) {
-        const int64_t lim = (p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1) - n0;
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
+        for (int c = 64; c < 128; ++c)
           if (c > lim) sr[c] = __float_as_uint(-INFINITY);
       }
-      float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; c += 8) {
+      for (int c = 64; c < 128; c += 8) {
         a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
         a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
         a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
@@ -385,6 +398,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (mx > m + kRescaleLog2) {  // first tile: m = -inf
         alpha = ptx::ex2_approx(m - mx);
         m = mx;
+      }
+      // P_j overwrites P_{j-1}: wait until P_{j-1}.V has completed (which also
+      // makes O final for the rescale); P is then stored in 16-column pieces
+      // as it is produced.
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(j - 1) & 1, p.status));
+        if (!ok) break;
+        ptx::tc_fence_after();
       }
       const uint64_t nm = ptx::f2_pack(-m, -m);
       uint64_t s0 = 0, s1 = 0;  // bit pattern 0 == (0.f, 0.f)
@@ -404,6 +425,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float p0, p1;
         ptx::f2_unpack(p2, p0, p1);
         pk[c] = ptx::pack_bf16x2(p0, p1);
+        if ((c & 15) == 15)
+          ptx::tmem_st16(lane_base + cP + c - 15, *reinterpret_cast<uint32_t(*)[16]>(&pk[c - 15]));
       }
       {
         float x0, x1;
@@ -411,14 +434,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         l = l * alpha + (x0 + x1);
       }
 
-      // P_j overwrites P_{j-1}: wait until P_{j-1}.V has completed (which also
-      // makes O final for the rescale).
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(j - 1) & 1, p.status));
-        if (!ok) break;
-        ptx::tc_fence_after();
-      }
-      ptx::tmem_st_32x32b_x64(lane_base + cP, pk);
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         uint32_t o[64];
         ptx::tmem_ld_32x32b_x64(lane_base + cO, o);

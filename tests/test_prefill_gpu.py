@@ -144,8 +144,9 @@ def test_bf16_sizes(wf, s):
 
 # The library runs the one-tile kernel when ceil(Sq/256)*B*H is below the SM
 # count (148 on B200) and the two-tile kernel otherwise: the small cases above
-# take the first, the B*H = 160 cases below the second.
-@pytest.mark.parametrize("s", [1, 129, 256, 300, 1000])
+# take the first, the B*H = 160 cases below the second (one CTA per SM walks
+# 160 to 640 work items of 256 query rows, so each CTA runs several).
+@pytest.mark.parametrize("s", [1, 100, 129, 256, 300, 1000])
 def test_bf16_two_tile_kernel_sizes(wf, s):
     q, k, v = (_randn((2, 80, s, 64), 450 + i, torch.bfloat16) for i in range(3))
     out = wf.attention(q.cuda(), k.cuda(), v.cuda()).float().cpu().numpy()

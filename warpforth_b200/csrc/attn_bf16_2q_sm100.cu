@@ -5,8 +5,8 @@
 // 128-row tiles A and B that share every K/V tile loaded by TMA (half the
 // L2 -> shared-memory traffic per FLOP of one tile per CTA).
 //
-//   warp 1 (TMA, K)   Q_A, Q_B once; then K_j tiles into a 4-deep ring
-//   warp 2 (TMA, V)   V_j tiles into their own 4-deep ring.  K and V have
+//   warp 1 (TMA, K)   Q_A, Q_B of each work item (two slots); K_j tiles into a 3-deep ring
+//   warp 2 (TMA, V)   V_j tiles into their own 3-deep ring.  K and V have
 //                     separate producers so a K load never waits for a V
 //                     slot (V slots free only after P.V, later than K slots).
 //   warp 0 (MMA, QK)  S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T, each as soon as
@@ -50,7 +50,7 @@ namespace {
 constexpr int kBM = 128;  // rows per query tile (= TMEM lanes)
 constexpr int kBN = 128;  // keys per K/V tile
 constexpr int kD = 64;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kSoftmaxWarps = 8;  // 2 tiles x 4 warps of 32 rows
 // Helper warps 0-3 (one per scheduler), softmax warps 4-11.
 constexpr int kMmaQkWarp = 0, kTmaKWarp = 1, kTmaVWarp = 2, kMmaPvWarp = 3, kFirstSoftmaxWarp = 4;
@@ -62,13 +62,16 @@ constexpr float kRescaleLog2 = 8.f;
 constexpr int kPolyPairsOf8 = 2;  // exp2 pairs per 8 pairs on the polynomial (25%)
 
 struct Smem {
-  uint8_t q[2][kTileBytes];
+  uint8_t q[2][2][kTileBytes];  // [slot][tile A/B]: Q of two consecutive work items
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint64_t q_full;
+  // Output staging, one 32-row x 128-byte slab per softmax warp in the TMA
+  // 128-byte-swizzle layout (16-byte chunk c of row r at c ^ (r % 8)).
+  uint8_t ostage[kSoftmaxWarps][32 * 128];
+  uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
+  uint64_t s_full[2], s_free[2], p_full[2], o_done[2], o_free[2];
   uint64_t drain[2];  // per MMA-issuing thread
 #ifdef WFATTN_TRACE
   unsigned long long tl[24][64];  // cycle timeline of CTA 0 (trace builds only)
@@ -81,12 +84,48 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 struct Params {
   int64_t B, H, Sq, Sk;
   int64_t n_pairs;  // 256-row query blocks per (batch, head)
+  int64_t n_items;  // n_pairs * B * H
   char *o;
   int64_t os_b, os_h, os_s;
   float scale_log2;
   int causal;
   unsigned int *status;
 };
+
+// One work item: 256 query rows (tiles A and B) of one (batch, head).
+struct Item {
+  int b, h;
+  int64_t q0;
+  int qrows[2], nkv[2], n_kv;
+};
+
+// Items are numbered heaviest first (the causal blocks nearest the end of the
+// sequence see the most keys).  CTA i takes item r*G + i in even rounds r and
+// r*G + (G-1-i) in odd ones (G = grid size): the snake order evens out the
+// CTAs' totals.  Returns false past the last item.
+__device__ __forceinline__ bool item_of(const Params &p, int k, Item &it) {
+  // 32-bit arithmetic: the launcher keeps n_items below 2^31.
+  const uint32_t G = gridDim.x;
+  const uint32_t idx = (uint32_t)k * G + ((k & 1) ? G - 1 - blockIdx.x : blockIdx.x);
+  if ((int64_t)idx >= p.n_items) return false;
+  const uint32_t BH = (uint32_t)(p.B * p.H), H = (uint32_t)p.H;
+  const uint32_t blk = idx / BH, bh = idx - blk * BH;
+  const int64_t qp = p.n_pairs - 1 - blk;
+  it.b = (int)(bh / H);
+  it.h = (int)(bh - (uint32_t)it.b * H);
+  it.q0 = qp * 2 * kBM;
+  const int64_t off = p.Sk - p.Sq;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int64_t r0 = it.q0 + t * kBM;
+    it.qrows[t] = r0 < p.Sq ? (int)imin64(kBM, p.Sq - r0) : 0;
+    int64_t kend = p.Sk;
+    if (p.causal && it.qrows[t] > 0) kend = imin64(p.Sk, r0 + it.qrows[t] - 1 + off + 1);
+    it.nkv[t] = it.qrows[t] > 0 ? (int)((kend + kBN - 1) / kBN) : 0;
+  }
+  it.n_kv = max(it.nkv[0], it.nkv[1]);
+  return true;
+}
 
 #ifdef WFATTN_TRACE
 #define TL(e, j)                                                  \
@@ -140,33 +179,21 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_bf16_2q_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                           const __grid_constant__ CUtensorMap tm_v,
+                           const __grid_constant__ CUtensorMap tm_o, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (ptx::timeout_flagged(p.status)) return;  // sticky until the host clears it
   if (threadIdx.x == 0) trace(0, 1);
-
-  const int64_t BH = p.B * p.H;
-  const int64_t qp = p.n_pairs - 1 - (int64_t)blockIdx.x / BH;  // heaviest first
-  const int64_t bh = (int64_t)blockIdx.x % BH;
-  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
-  const int64_t q0 = qp * 2 * kBM;
   const int64_t off = p.Sk - p.Sq;
-  int qrows[2], nkv[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int64_t r0 = q0 + t * kBM;
-    qrows[t] = r0 < p.Sq ? (int)imin64(kBM, p.Sq - r0) : 0;
-    int64_t kend = p.Sk;
-    if (p.causal && qrows[t] > 0) kend = imin64(p.Sk, r0 + qrows[t] - 1 + off + 1);
-    nkv[t] = qrows[t] > 0 ? (int)((kend + kBN - 1) / kBN) : 0;
-  }
-  const int n_kv = max(nkv[0], nkv[1]);
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(ptx::smem_u32(&sm.q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(ptx::smem_u32(&sm.q_full[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sm.q_empty[i]), 1);
+    }
     for (int i = 0; i < kStages; ++i) {
       ptx::mbar_init(ptx::smem_u32(&sm.k_full[i]), 1);
       ptx::mbar_init(ptx::smem_u32(&sm.k_empty[i]), 1);
@@ -178,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&sm.s_free[t]), kBM);
       ptx::mbar_init(ptx::smem_u32(&sm.p_full[t]), kBM);
       ptx::mbar_init(ptx::smem_u32(&sm.o_done[t]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sm.o_free[t]), kBM);
     }
     ptx::mbar_init(ptx::smem_u32(&sm.drain[0]), 1);
     ptx::mbar_init(ptx::smem_u32(&sm.drain[1]), 1);
@@ -189,7 +217,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tm_q);
     ptx::prefetch_tmap(&tm_k);
   }
-  if (warp == kTmaVWarp && lane == 0) ptx::prefetch_tmap(&tm_v);
+  if (warp == kTmaVWarp && lane == 0) {
+    ptx::prefetch_tmap(&tm_v);
+    ptx::prefetch_tmap(&tm_o);
+  }
   if (warp == kMmaQkWarp) {
     if (lane == 0) trace(1, 1);
     ptx::tmem_alloc(ptx::smem_u32(&sm.tmem_base), kTmemCols);
@@ -208,6 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     trace(7, tmem);
   }
 
+  // Every role walks the same item sequence; ring and barrier phases are
+  // counted across items, so the next item's loads and S = QK^T overlap the
+  // current item's last iterations and its output.
   if (warp == kTmaKWarp || warp == kTmaVWarp) {
     // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
@@ -216,35 +250,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t *full = is_k ? sm.k_full : sm.v_full;
       uint64_t *empty = is_k ? sm.k_empty : sm.v_empty;
       uint8_t(*ring)[kTileBytes] = is_k ? sm.k : sm.v;
-      const uint32_t qf = ptx::smem_u32(&sm.q_full);
-      if (is_k) {
-        const int nq = qrows[1] > 0 ? 2 : 1;
-        ptx::mbar_arrive_expect_tx(qf, kTileBytes * nq);
-        for (int t = 0; t < nq; ++t)
-          ptx::tma_load_4d(ptx::smem_u32(sm.q[t]), &tm_q, 0, (int)(q0 + t * kBM), h, b, qf);
-      }
-      trace(2, 1);
-      int issued = 0;  // loads issued so far (tile index + 1)
-      for (int j = 0; j < n_kv && !aborted(sm); ++j) {
-        const int st = j % kStages;
-        const uint32_t use = (uint32_t)(j / kStages);
-        if (j >= kStages &&
-            !ptx::mbar_wait(ptx::smem_u32(&empty[st]), (use - 1) & 1, p.status)) {
-          set_abort(sm);
-          break;
+      int issued = 0;   // ring loads so far
+      int q_items = 0;  // items whose Q was loaded
+      bool ok = true;
+      Item it;
+      for (int k = 0; ok && item_of(p, k, it); ++k) {
+        if (is_k) {
+          // Q of this item into slot k & 1, once the QKs of item k-2 are done.
+          const int slot = k & 1;
+          if (k >= 2 && !ptx::mbar_wait(ptx::smem_u32(&sm.q_empty[slot]),
+                                        (uint32_t)((k >> 1) - 1) & 1, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t qf = ptx::smem_u32(&sm.q_full[slot]);
+          const int nq = it.qrows[1] > 0 ? 2 : 1;
+          ptx::mbar_arrive_expect_tx(qf, kTileBytes * nq);
+          for (int t = 0; t < nq; ++t)
+            ptx::tma_load_4d(ptx::smem_u32(sm.q[slot][t]), &tm_q, 0, (int)(it.q0 + t * kBM), it.h,
+                             it.b, qf);
+          q_items = k + 1;
         }
-        const uint32_t fb = ptx::smem_u32(&full[st]);
-        ptx::mbar_arrive_expect_tx(fb, kTileBytes);
-        ptx::tma_load_4d(ptx::smem_u32(ring[st]), tm, 0, j * kBN, h, b, fb);
-        issued = j + 1;
-        if (is_k) TL(20, j);
+        for (int j = 0; j < it.n_kv; ++j) {
+          const int st = issued % kStages;
+          if (aborted(sm) ||
+              (issued >= kStages && !ptx::mbar_wait(ptx::smem_u32(&empty[st]),
+                                                    (uint32_t)(issued / kStages - 1) & 1,
+                                                    p.status))) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = ptx::smem_u32(&full[st]);
+          ptx::mbar_arrive_expect_tx(fb, kTileBytes);
+          ptx::tma_load_4d(ptx::smem_u32(ring[st]), tm, 0, j * kBN, it.h, it.b, fb);
+          if (is_k) TL(20, issued);
+          ++issued;
+        }
       }
-      if (aborted(sm)) {
+      trace(2, ok ? 5 : 6);
+      if (!ok) {
+        set_abort(sm);
         // Drain: every load this thread issued must land before the CTA exits.
-        if (is_k) ptx::mbar_wait_drain(qf, 0);
+        for (int i = (int)imin64(q_items, 2); i > 0; --i) {
+          const int u = q_items - i;
+          ptx::mbar_wait_drain(ptx::smem_u32(&sm.q_full[u & 1]), (uint32_t)(u >> 1) & 1);
+        }
         for (int i = (int)imin64(issued, kStages); i > 0; --i) {
-          const int t = issued - i;
-          ptx::mbar_wait_drain(ptx::smem_u32(&full[t % kStages]), (uint32_t)(t / kStages) & 1);
+          const int u = issued - i;
+          ptx::mbar_wait_drain(ptx::smem_u32(&full[u % kStages]), (uint32_t)(u / kStages) & 1);
         }
       }
     }
@@ -259,72 +312,84 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(kBM, kD, 0, 1);
       // Descriptors: constant high halves; low halves = start address >> 4
-      // (a K step adds 32 B for Q/K, 2 KB for V; a ring stage adds 16 KB).
-      const uint64_t dq0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.q[0]), 16, 1024);
-      const uint64_t dq1 = ptx::smem_desc_sw128(ptx::smem_u32(sm.q[1]), 16, 1024);
+      // (a K step adds 32 B for Q/K, 2 KB for V; a ring stage or Q tile adds 16 KB).
+      const uint64_t dq0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.q[0][0]), 16, 1024);
       const uint64_t dk0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.k[0]), 16, 1024);
       const uint64_t dv0 = ptx::smem_desc_sw128(ptx::smem_u32(sm.v[0]), kTileBytes, 1024);
       const uint32_t hi_qk = (uint32_t)(dk0 >> 32), hi_v = (uint32_t)(dv0 >> 32);
-      const uint32_t qlo[2] = {(uint32_t)dq0, (uint32_t)dq1};
-      const uint32_t klo0 = (uint32_t)dk0, vlo0 = (uint32_t)dv0;
+      const uint32_t qlo0 = (uint32_t)dq0, klo0 = (uint32_t)dk0, vlo0 = (uint32_t)dv0;
       constexpr uint32_t kStageLo = kTileBytes >> 4;
-      bool ok = n_kv > 0 && (!is_qk || ptx::mbar_wait(ptx::smem_u32(&sm.q_full), 0, p.status));
-      trace(1, ok ? 3 : 4);
+      int ring = 0;                 // K (V) tiles consumed so far
+      int n_mma[2] = {0, 0};        // S (P.V) products issued per tile half
+      int n_items_t[2] = {0, 0};    // items with rows per tile half (P.V thread)
+      bool ok = true;
+      trace(1, 3);
 
-      // S_t = Q_t K_j^T once softmax t has read S_t(j-1) out of TMEM.
-      auto issue_qk = [&](int t, int j) -> bool {
-        if (j > 0 &&
-            !ptx::mbar_wait(ptx::smem_u32(&sm.s_free[t]), (uint32_t)(j - 1) & 1, p.status))
-          return false;
-        TL(t ? 13 : 5, j);
-        ptx::tc_fence_after();
-        const uint32_t tS = tmem + kColS0 + 128 * t, qa = qlo[t];
-        const uint32_t kb = klo0 + (j % kStages) * kStageLo;
-        ptx::mma_ss_lh<false>(tS, qa, hi_qk, kb, hi_qk, idesc_qk);
-        ptx::mma_ss_lh<true>(tS, qa + 2, hi_qk, kb + 2, hi_qk, idesc_qk);
-        ptx::mma_ss_lh<true>(tS, qa + 4, hi_qk, kb + 4, hi_qk, idesc_qk);
-        ptx::mma_ss_lh<true>(tS, qa + 6, hi_qk, kb + 6, hi_qk, idesc_qk);
-        TL(t ? 14 : 6, j);
-        ptx::tc_commit(ptx::smem_u32(&sm.s_full[t]));
-        TL(t, j);
-        return true;
-      };
-      // O_t += P_t(j) V_j once softmax t has written P_t(j) (and rescaled O_t).
-      auto issue_pv = [&](int t, int j) -> bool {
-        if (!ptx::mbar_wait(ptx::smem_u32(&sm.p_full[t]), (uint32_t)j & 1, p.status)) return false;
-        TL(t ? 15 : 9, j);
-        ptx::tc_fence_after();
-        const uint32_t tO = tmem + kColO0 + 64 * t, tP = tmem + kColP0 + 64 * t;
-        const uint32_t vb = vlo0 + (j % kStages) * kStageLo;
-        if (j == 0)
-          ptx::mma_ts_lh<false>(tO, tP, vb, hi_v, idesc_pv);
-        else
-          ptx::mma_ts_lh<true>(tO, tP, vb, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 8, vb + 128, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 16, vb + 256, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 24, vb + 384, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 32, vb + 512, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 40, vb + 640, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 48, vb + 768, hi_v, idesc_pv);
-        ptx::mma_ts_lh<true>(tO, tP + 56, vb + 896, hi_v, idesc_pv);
-        TL(t ? 17 : 11, j);
-        ptx::tc_commit(ptx::smem_u32(&sm.o_done[t]));
-        TL(2 + t, j);
-        return true;
-      };
-
-      uint64_t *full = is_qk ? sm.k_full : sm.v_full;
-      uint64_t *empty = is_qk ? sm.k_empty : sm.v_empty;
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % kStages;
-        ok = ptx::mbar_wait(ptx::smem_u32(&full[st]), (uint32_t)(j / kStages) & 1, p.status);
-        TL(is_qk ? 18 : 19, j);
+      Item it;
+      for (int k = 0; ok && item_of(p, k, it); ++k) {
+        const int slot = k & 1;
+        if (is_qk)
+          ok = ptx::mbar_wait(ptx::smem_u32(&sm.q_full[slot]), (uint32_t)(k >> 1) & 1, p.status);
+        for (int j = 0; ok && j < it.n_kv; ++j, ++ring) {
+          const int st = ring % kStages;
+          uint64_t *full = is_qk ? sm.k_full : sm.v_full;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[st]), (uint32_t)(ring / kStages) & 1, p.status);
+          TL(is_qk ? 18 : 19, ring);
 #pragma unroll
-        for (int t = 0; t < 2; ++t)
-          if (ok && j < nkv[t]) ok = is_qk ? issue_qk(t, j) : issue_pv(t, j);
-        // Frees the K (V) stage once the MMAs reading it have completed.
-        if (ok) ptx::tc_commit(ptx::smem_u32(&empty[st]));
-        trace(1, 100 + j);
+          for (int t = 0; t < 2; ++t) {
+            if (!ok || j >= it.nkv[t]) continue;
+            const int n = n_mma[t];
+            if (is_qk) {
+              // S_t is free once softmax t has read the previous S_t out of TMEM.
+              if (n > 0)
+                ok = ptx::mbar_wait(ptx::smem_u32(&sm.s_free[t]), (uint32_t)(n - 1) & 1, p.status);
+              if (!ok) continue;
+              ptx::tc_fence_after();
+              const uint32_t tS = tmem + kColS0 + 128 * t;
+              const uint32_t qa = qlo0 + (2 * slot + t) * kStageLo;
+              const uint32_t kb = klo0 + st * kStageLo;
+              ptx::mma_ss_lh<false>(tS, qa, hi_qk, kb, hi_qk, idesc_qk);
+              ptx::mma_ss_lh<true>(tS, qa + 2, hi_qk, kb + 2, hi_qk, idesc_qk);
+              ptx::mma_ss_lh<true>(tS, qa + 4, hi_qk, kb + 4, hi_qk, idesc_qk);
+              ptx::mma_ss_lh<true>(tS, qa + 6, hi_qk, kb + 6, hi_qk, idesc_qk);
+              ptx::tc_commit(ptx::smem_u32(&sm.s_full[t]));
+              TL(t, n);
+            } else {
+              // The first P.V of an item overwrites O_t: softmax t must have
+              // read the previous item's O_t.  Every P.V needs P_t written.
+              if (j == 0 && n_items_t[t] > 0)
+                ok = ptx::mbar_wait(ptx::smem_u32(&sm.o_free[t]),
+                                    (uint32_t)(n_items_t[t] - 1) & 1, p.status);
+              if (ok)
+                ok = ptx::mbar_wait(ptx::smem_u32(&sm.p_full[t]), (uint32_t)n & 1, p.status);
+              if (!ok) continue;
+              ptx::tc_fence_after();
+              const uint32_t tO = tmem + kColO0 + 64 * t, tP = tmem + kColP0 + 64 * t;
+              const uint32_t vb = vlo0 + st * kStageLo;
+              if (j == 0)
+                ptx::mma_ts_lh<false>(tO, tP, vb, hi_v, idesc_pv);
+              else
+                ptx::mma_ts_lh<true>(tO, tP, vb, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 8, vb + 128, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 16, vb + 256, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 24, vb + 384, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 32, vb + 512, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 40, vb + 640, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 48, vb + 768, hi_v, idesc_pv);
+              ptx::mma_ts_lh<true>(tO, tP + 56, vb + 896, hi_v, idesc_pv);
+              ptx::tc_commit(ptx::smem_u32(&sm.o_done[t]));
+              TL(2 + t, n);
+            }
+            n_mma[t] = n + 1;
+          }
+          // Frees the K (V) stage once the MMAs reading it have completed.
+          if (ok) ptx::tc_commit(ptx::smem_u32(&(is_qk ? sm.k_empty : sm.v_empty)[st]));
+          trace(1, 100 + ring);
+        }
+        // Frees the Q slot once this item's S products have completed.
+        if (ok && is_qk) ptx::tc_commit(ptx::smem_u32(&sm.q_empty[slot]));
+#pragma unroll
+        for (int t = 0; t < 2; ++t) n_items_t[t] += it.nkv[t] > 0;
       }
       trace(1, ok ? 5 : 6);
       if (!ok) {
@@ -336,149 +401,177 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warps 3-10
+    // ------------------------------------------------------------ softmax warps 4-11
     const int t = (warp - kFirstSoftmaxWarp) >> 2;  // query tile
-    const int row = 32 * (warp & 3) + lane;       // TMEM lane == row within the tile
-    const int n = t ? nkv[1] : nkv[0];
-    const int rows = t ? qrows[1] : qrows[0];
+    const int row = 32 * (warp & 3) + lane;         // TMEM lane == row within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const uint32_t cS = kColS0 + 128 * t, cP = kColP0 + 64 * t, cO = kColO0 + 64 * t;
-    const int64_t grow = q0 + t * kBM + row;  // global query row
     const uint32_t bar_s_full = ptx::smem_u32(&sm.s_full[t]);
     const uint32_t bar_s_free = ptx::smem_u32(&sm.s_free[t]);
     const uint32_t bar_p_full = ptx::smem_u32(&sm.p_full[t]);
     const uint32_t bar_o_done = ptx::smem_u32(&sm.o_done[t]);
+    const uint32_t bar_o_free = ptx::smem_u32(&sm.o_free[t]);
+    uint8_t *stage = sm.ostage[warp - kFirstSoftmaxWarp];
     const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
-    float m = -INFINITY;  // running offset of this row (log2 units)
-    float l = 0.f;        // running sum of 2^(x - m)
-    bool ok = n > 0;
-    for (int j = 0; j < n; ++j) {
-      ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_s_full, (uint32_t)j & 1, p.status));
-      if (!ok) break;
-      ptx::tc_fence_after();
-      uint32_t sr[128];
-      const int64_t n0 = (int64_t)j * kBN;
-      const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q0 + t * kBM + off);
-      const int64_t lim = masked ? (p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1) - n0 : 127;
-      float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
-      ptx::tmem_ld_32x32b_x64(lane_base + cS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
-      ptx::tmem_wait_ld();
-      ptx::tmem_ld_32x32b_x64(lane_base + cS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
-      // the first half's max overlaps the second half's load
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
-      }
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-        a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-        a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-        a3 = ptx::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-      }
-      ptx::tmem_wait_ld();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(bar_s_free);
-      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(4 + 4 * t, j);
-      if (masked) {
-#pragma unroll
-        for (int c = 64; c < 128; ++c)
-          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
-      }
-#pragma unroll
-      for (int c = 64; c < 128; c += 8) {
-        a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-        a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-        a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-        a3 = ptx::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-      }
-      const float mx = fmaxf(ptx::fmax3(a0, a1, a2), a3) * p.scale_log2;
-      float alpha = 1.f;
-      if (mx > m + kRescaleLog2) {  // first tile: m = -inf
-        alpha = ptx::ex2_approx(m - mx);
-        m = mx;
-      }
-      // P_j overwrites P_{j-1}: wait until P_{j-1}.V has completed (which also
-      // makes O final for the rescale); P is then stored in 16-column pieces
-      // as it is produced.
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(j - 1) & 1, p.status));
+    int ns = 0;  // S tiles of this tile half consumed so far (= P tiles written)
+    bool ok = true;
+    Item it;
+    for (int k = 0; ok && item_of(p, k, it); ++k) {
+      const int n = t ? it.nkv[1] : it.nkv[0];
+      if (n == 0) continue;  // ragged last block: this half has no rows
+      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 17 : 11, k);
+      const int64_t q_tile = it.q0 + t * kBM;
+      const int64_t grow = q_tile + row;  // global query row
+      float m = -INFINITY;  // running offset of this row (log2 units)
+      float l = 0.f;        // running sum of 2^(x - m)
+      for (int j = 0; j < n; ++j, ++ns) {
+        ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_s_full, (uint32_t)ns & 1, p.status));
         if (!ok) break;
         ptx::tc_fence_after();
-      }
-      const uint64_t nm = ptx::f2_pack(-m, -m);
-      uint64_t s0 = 0, s1 = 0;  // bit pattern 0 == (0.f, 0.f)
-      // P row packed in place: pair c reads sr[2c], sr[2c+1] and writes sr[c],
-      // which pair c/2 has already read.
-      uint32_t(&pk)[64] = *reinterpret_cast<uint32_t(*)[64]>(&sr[0]);
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const uint64_t x2 = ptx::f2_fma(
-            ptx::f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), c2, nm);
-        const bool poly = (c & 7) < kPolyPairsOf8;
-        const uint64_t p2 = poly ? exp2_poly2(x2) : exp2_mufu2(x2);
-        if (c & 1)
-          s1 = ptx::f2_add(s1, p2);
-        else
-          s0 = ptx::f2_add(s0, p2);
-        float p0, p1;
-        ptx::f2_unpack(p2, p0, p1);
-        pk[c] = ptx::pack_bf16x2(p0, p1);
-        if ((c & 15) == 15)
-          ptx::tmem_st16(lane_base + cP + c - 15, *reinterpret_cast<uint32_t(*)[16]>(&pk[c - 15]));
-      }
-      {
-        float x0, x1;
-        ptx::f2_unpack(ptx::f2_add(s0, s1), x0, x1);
-        l = l * alpha + (x0 + x1);
-      }
-
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        uint32_t o[64];
-        ptx::tmem_ld_32x32b_x64(lane_base + cO, o);
+        uint32_t sr[128];
+        const int64_t n0 = (int64_t)j * kBN;
+        const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q_tile + off);
+        const int64_t lim =
+            masked ? (p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1) - n0 : 127;
+        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+        ptx::tmem_ld_32x32b_x64(lane_base + cS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
         ptx::tmem_wait_ld();
-        const uint64_t a2 = ptx::f2_pack(alpha, alpha);
+        ptx::tmem_ld_32x32b_x64(lane_base + cS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+        // the first half's max overlaps the second half's load
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          float w0, w1;
-          ptx::f2_unpack(
-              ptx::f2_mul(ptx::f2_pack(__uint_as_float(o[c]), __uint_as_float(o[c + 1])), a2),
-              w0, w1);
-          o[c] = __float_as_uint(w0);
-          o[c + 1] = __float_as_uint(w1);
+          for (int c = 0; c < 64; ++c)
+            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
         }
-        ptx::tmem_st_32x32b_x64(lane_base + cO, o);
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          a3 = ptx::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+        }
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar_s_free);
+        if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(4 + 4 * t, ns);
+        if (masked) {
+#pragma unroll
+          for (int c = 64; c < 128; ++c)
+            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int c = 64; c < 128; c += 8) {
+          a0 = ptx::fmax3(a0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          a1 = ptx::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          a2 = ptx::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          a3 = ptx::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+        }
+        const float mx = fmaxf(ptx::fmax3(a0, a1, a2), a3) * p.scale_log2;
+        float alpha = 1.f;
+        if (mx > m + kRescaleLog2) {  // first tile: m = -inf
+          alpha = ptx::ex2_approx(m - mx);
+          m = mx;
+        }
+        // P overwrites the previous P of this tile half (possibly the previous
+        // item's last): wait until that P.V has completed (which also makes O
+        // final for the rescale); P is then stored in 16-column pieces as it
+        // is produced.
+        if (ns > 0) {
+          ok = __all_sync(0xffffffffu,
+                          ptx::mbar_wait(bar_o_done, (uint32_t)(ns - 1) & 1, p.status));
+          if (!ok) break;
+          ptx::tc_fence_after();
+        }
+        const uint64_t nm = ptx::f2_pack(-m, -m);
+        uint64_t s0 = 0, s1 = 0;  // bit pattern 0 == (0.f, 0.f)
+        // P row packed in place: pair c reads sr[2c], sr[2c+1] and writes sr[c],
+        // which pair c/2 has already read.
+        uint32_t(&pk)[64] = *reinterpret_cast<uint32_t(*)[64]>(&sr[0]);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const uint64_t x2 = ptx::f2_fma(
+              ptx::f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), c2, nm);
+          const bool poly = (c & 7) < kPolyPairsOf8;
+          const uint64_t p2 = poly ? exp2_poly2(x2) : exp2_mufu2(x2);
+          if (c & 1)
+            s1 = ptx::f2_add(s1, p2);
+          else
+            s0 = ptx::f2_add(s0, p2);
+          float p0, p1;
+          ptx::f2_unpack(p2, p0, p1);
+          pk[c] = ptx::pack_bf16x2(p0, p1);
+          if ((c & 15) == 15)
+            ptx::tmem_st16(lane_base + cP + c - 15,
+                           *reinterpret_cast<uint32_t(*)[16]>(&pk[c - 15]));
+        }
+        {
+          float x0, x1;
+          ptx::f2_unpack(ptx::f2_add(s0, s1), x0, x1);
+          l = l * alpha + (x0 + x1);
+        }
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          uint32_t o[64];
+          ptx::tmem_ld_32x32b_x64(lane_base + cO, o);
+          ptx::tmem_wait_ld();
+          const uint64_t a2 = ptx::f2_pack(alpha, alpha);
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            float w0, w1;
+            ptx::f2_unpack(
+                ptx::f2_mul(ptx::f2_pack(__uint_as_float(o[c]), __uint_as_float(o[c + 1])), a2),
+                w0, w1);
+            o[c] = __float_as_uint(w0);
+            o[c + 1] = __float_as_uint(w1);
+          }
+          ptx::tmem_st_32x32b_x64(lane_base + cO, o);
+        }
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar_p_full);
+        if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(12 + 4 * t, ns);
+        if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, 100 + ns);
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(bar_p_full);
-      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(12 + 4 * t, j);
-      if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, 100 + j);
-    }
-    if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(n - 1) & 1, p.status));
-    if (ok) {
+      if (!ok) break;
+      // ---- output of this item: O_t / l once the last P.V has completed.
+      // O_t is handed back to the P.V thread as soon as it is in registers;
+      // the rows go out through this warp's staging slab and one TMA store
+      // (rows past Sq are clipped by the tensor map).
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(ns - 1) & 1, p.status));
+      if (!ok) break;
+      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 13 : 5, k);
       ptx::tc_fence_after();
-      const float inv = 1.f / l;
       uint32_t o[64];
       ptx::tmem_ld_32x32b_x64(lane_base + cO, o);
       ptx::tmem_wait_ld();
-      if (row < rows) {
-        char *dst = p.o + 2 * (b * p.os_b + h * p.os_h + grow * p.os_s);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar_o_free);
+      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 14 : 6, k);
+      const float inv = 1.f / l;
+      // the previous item's store must have finished reading the slab
+      if (lane == 0) ptx::bulk_wait_group_read0();
+      __syncwarp();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 w;
-          const uint32_t *src = &o[8 * c];
-          w.x = ptx::pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-          w.y = ptx::pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-          w.z = ptx::pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-          w.w = ptx::pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-          reinterpret_cast<uint4 *>(dst)[c] = w;
-        }
+      for (int c = 0; c < 8; ++c) {
+        uint4 w;
+        const uint32_t *src = &o[8 * c];
+        w.x = ptx::pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+        w.y = ptx::pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+        w.z = ptx::pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+        w.w = ptx::pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        *reinterpret_cast<uint4 *>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = w;
       }
-    } else if (n > 0) {
-      set_abort(sm);
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::tma_store_4d(&tm_o, ptx::smem_u32(stage), 0, (int)(q_tile + 32 * (warp & 3)), it.h,
+                          it.b);
+        ptx::bulk_commit_group();
+      }
+      if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 15 : 9, k);
     }
+    // Outstanding output stores must complete before the CTA exits.
+    if (lane == 0) ptx::bulk_wait_group0();
+    if (!ok) set_abort(sm);
     if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, ok ? 5 : 6);
   }
 
@@ -506,10 +599,11 @@ cudaError_t set_trace_prefill_2q(void *p) { return set_trace_symbol(p); }
 cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
                                    cudaStream_t stream) {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if (!make_bf16_map_64x128(&tq, a.q, a.B, a.H, a.Sq, a.qs) ||
       !make_bf16_map_64x128(&tk, a.k, a.B, a.H, a.Sk, a.ks) ||
-      !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
+      !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs) ||
+      !make_bf16_map_64xR(&to, a.o, a.B, a.H, a.Sq, a.os, 32))
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
     return cudaErrorInvalidValue;
@@ -529,9 +623,11 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   p.scale_log2 = (float)((double)a.scale * 1.4426950408889634);
   p.causal = a.causal;
   p.status = dev.status;
-  const int64_t blocks = p.n_pairs * a.B * a.H;
-  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+  p.n_items = p.n_pairs * a.B * a.H;
+  if (p.n_items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  // Persistent: one CTA per SM walks the items (fewer CTAs for small problems).
+  const int64_t blocks = p.n_items < dev.sm_count ? p.n_items : dev.sm_count;
+  prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }
 

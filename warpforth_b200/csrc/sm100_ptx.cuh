@@ -172,6 +172,32 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *m, 
       : "memory");
 }
 
+// Tiled TMA store shared -> global (no multicast).  Rows past the tensor's
+// extent are not written.  Completion is tracked per thread with bulk groups.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *m, uint32_t src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+      ::"l"(reinterpret_cast<uint64_t>(m)), "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until this thread's bulk groups have finished READING shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until this thread's bulk groups have completed (writes performed).
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA) before a TMA store reads them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Untiled bulk copy global -> shared (both 16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
                                           uint32_t bar) {

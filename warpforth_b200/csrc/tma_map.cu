@@ -26,8 +26,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-bool make_bf16_map_64x128(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
-                          const Strides3 &st) {
+bool make_bf16_map_64xR(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
+                        const Strides3 &st, int box_rows) {
   auto enc = encode_fn();
   if (!enc) return false;
   const cuuint64_t dims[4] = {64, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
@@ -37,13 +37,18 @@ bool make_bf16_map_64x128(CUtensorMap *m, const void *base, int64_t B, int64_t H
   // (TMA wants non-zero multiples of 16 bytes).
   for (int i = 0; i < 3; ++i)
     if (extent[i] == 1 && strides[i] == 0) strides[i] = 128;
-  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r =
       enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box,
           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+bool make_bf16_map_64x128(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
+                          const Strides3 &st) {
+  return make_bf16_map_64xR(m, base, B, H, S, st, 128);
 }
 
 }  // namespace wfattn

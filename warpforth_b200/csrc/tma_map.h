@@ -14,5 +14,8 @@ namespace wfattn {
 // point is unavailable or the encoding is rejected.
 bool make_bf16_map_64x128(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
                           const Strides3 &st);
+// The same with a box of {64, box_rows, 1, 1} (box_rows <= 256).
+bool make_bf16_map_64xR(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
+                        const Strides3 &st, int box_rows);
 
 }  // namespace wfattn

@@ -172,8 +172,9 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
     const int64_t ext_q[3] = {batch, heads, seq_q}, ext_k[3] = {batch, heads, seq_k};
     for (int i = 0; i < 3; ++i) {
       const int64_t sq[3] = {a.qs.b, a.qs.h, a.qs.s}, sk[3] = {a.ks.b, a.ks.h, a.ks.s},
-                    sv[3] = {a.vs.b, a.vs.h, a.vs.s};
-      if ((ext_q[i] > 1 && sq[i] == 0) || (ext_k[i] > 1 && (sk[i] == 0 || sv[i] == 0)))
+                    sv[3] = {a.vs.b, a.vs.h, a.vs.s}, so[3] = {a.os.b, a.os.h, a.os.s};
+      if ((ext_q[i] > 1 && (sq[i] == 0 || so[i] == 0)) ||
+          (ext_k[i] > 1 && (sk[i] == 0 || sv[i] == 0)))
         return fail(WFATTN_INVALID_ARG, "bf16 path does not take zero (broadcast) strides");
     }
     // Two 128-row query tiles per CTA (one CTA per SM) halve the K/V traffic

@@ -607,8 +607,8 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
     return cudaErrorInvalidValue;
-  cudaError_t err = cudaFuncSetAttribute(
-      prefill_bf16_2q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_bf16_2q_kernel),
+                                     (int)kSmemBytes, dev.device);
   if (err != cudaSuccess) return err;
   Params p;
   p.B = a.B;

@@ -376,8 +376,8 @@ cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,
       !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff) return cudaErrorInvalidValue;
-  cudaError_t err = cudaFuncSetAttribute(
-      prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_bf16_kernel),
+                                     (int)kSmemBytes, dev.device);
   if (err != cudaSuccess) return err;
   Bf16Params p;
   p.B = a.B;

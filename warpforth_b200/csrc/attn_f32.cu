@@ -220,12 +220,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 template <int DP>
-cudaError_t launch_dp(const PrefillArgs &a, cudaStream_t stream) {
+cudaError_t launch_dp(const PrefillArgs &a, int device, cudaStream_t stream) {
   using L = F32Layout<DP>;
   static_assert(L::kBytes <= 227 * 1024, "f32 tile does not fit in shared memory");
-  cudaError_t err =
-      cudaFuncSetAttribute(prefill_f32_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)L::kBytes);
+  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_f32_kernel<DP>),
+                                     (int)L::kBytes, device);
   if (err != cudaSuccess) return err;
   const int64_t n_qtiles = (a.Sq + kBM - 1) / kBM;
   const int64_t blocks = n_qtiles * a.B * a.H;
@@ -247,10 +246,10 @@ cudaError_t launch_dp(const PrefillArgs &a, cudaStream_t stream) {
 
 }  // namespace
 
-cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &, cudaStream_t stream) {
-  if (a.D <= 64) return launch_dp<64>(a, stream);
-  if (a.D <= 128) return launch_dp<128>(a, stream);
-  return launch_dp<256>(a, stream);
+cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
+  if (a.D <= 64) return launch_dp<64>(a, dev.device, stream);
+  if (a.D <= 128) return launch_dp<128>(a, dev.device, stream);
+  return launch_dp<256>(a, dev.device, stream);
 }
 
 }  // namespace wfattn

@@ -489,8 +489,8 @@ cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaS
   const int64_t blocks = items < dev.sm_count ? items : dev.sm_count;
   static_assert(sizeof(DecSmem) <= 227 * 1024, "shared memory budget");
   const size_t smem = sizeof(DecSmem);
-  cudaError_t err = cudaFuncSetAttribute(decode_split_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(decode_split_kernel),
+                                     (int)smem, dev.device);
   if (err != cudaSuccess) return err;
   decode_split_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(p);
   err = cudaGetLastError();

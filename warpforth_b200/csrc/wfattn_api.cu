@@ -87,6 +87,25 @@ float resolve_scale(float scale, int64_t D) {
 
 }  // namespace
 
+namespace {
+struct SmemAttr {
+  const void *func;
+  int device, bytes;
+};
+std::mutex g_attr_mutex;
+std::vector<SmemAttr> g_attrs;
+}  // namespace
+
+cudaError_t ensure_smem_attr(const void *func, int bytes, int device) {
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  for (const SmemAttr &a : g_attrs)
+    if (a.func == func && a.device == device && a.bytes == bytes) return cudaSuccess;
+  const cudaError_t err =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) g_attrs.push_back(SmemAttr{func, device, bytes});
+  return err;
+}
+
 #ifdef WFATTN_TRACE
 cudaError_t set_trace_prefill_1q(void *p);
 cudaError_t set_trace_prefill_2q(void *p);

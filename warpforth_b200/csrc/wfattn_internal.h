@@ -52,6 +52,11 @@ struct DeviceInfo {
   unsigned int *status;  // device address of the status word
 };
 
+// Sets cudaFuncAttributeMaxDynamicSharedMemorySize of `func` on the current
+// device to `bytes` the first time it is asked for that (func, device, bytes)
+// and remembers it, so launches do not repeat the driver call.
+cudaError_t ensure_smem_attr(const void *func, int bytes, int device);
+
 cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream);
 // bf16 prefill: one 128-row query tile per CTA (2 CTAs per SM) ...
 cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,

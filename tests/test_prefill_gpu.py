@@ -157,6 +157,20 @@ def test_bf16_two_tile_kernel_sizes(wf, s):
         assert _bf16_rel_err(out.reshape(flat)[:, lo:hi], ref[:, lo:hi]) <= BF16_REL_TOL
 
 
+def test_bf16_two_tile_kernel_strided_views(wf):
+    # HF layout [B, S, H, D] viewed as [B, H, S, D] for q/k/v and for the output,
+    # which the two-tile kernel writes through a TMA tensor map
+    base = _randn((2, 300, 3, 80, 64), 470, torch.bfloat16).cuda()
+    q, k, v = (base[:, :, i].transpose(1, 2) for i in range(3))
+    dst = torch.full((2, 300, 80, 64), float("nan"), dtype=torch.bfloat16, device="cuda")
+    wf.attention(q, k, v, out=dst.transpose(1, 2))
+    out = dst.transpose(1, 2).float().cpu().numpy().reshape(1, 160, 300, 64)
+    qc, kc, vc = (t.contiguous().cpu() for t in (q, k, v))
+    ref = _oracle(qc, kc, vc, bh_range=(0, 4)).reshape(1, 160, 300, 64)
+    assert np.isfinite(out).all()
+    assert _bf16_rel_err(out[:, :4], ref[:, :4]) <= BF16_REL_TOL
+
+
 def test_bf16_two_tile_kernel_noncausal_cross_lengths(wf):
     qq = _randn((2, 80, 130, 64), 460, torch.bfloat16)
     kk, vv = (_randn((2, 80, 333, 64), 461 + i, torch.bfloat16) for i in range(2))

@@ -186,7 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (ptx::timeout_flagged(p.status)) return;  // sticky until the host clears it
-  if (threadIdx.x == 0) trace(0, 1);
+  if (threadIdx.x == 0) {
+    trace(0, 1);
+    trace(5, (unsigned int)ptx::globaltimer());  // CTA start (ns, low word)
+  }
   const int64_t off = p.Sk - p.Sq;
 
   if (threadIdx.x == 0) {
@@ -577,7 +580,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) trace(6, 1);
+  if (threadIdx.x == 0) {
+    trace(6, 1);
+    trace(7, (unsigned int)ptx::globaltimer());  // CTA end (ns, low word)
+  }
 #ifdef WFATTN_TRACE
   if (blockIdx.x == 0 && g_trace)
     for (int i = threadIdx.x; i < 24 * 64; i += kThreads)

@@ -7,11 +7,15 @@
 // 1e-5 absolute of the f64 reference for the GPT-2 head shapes; the tests
 // assert that bound against the CPU oracle.
 //
-// Shape of the work (one CTA = one 64-row query tile of one (batch, head)):
+// Shape of the work (one CTA = one query tile of 16*RPT rows of one (batch, head);
+// RPT = 8 rows per thread for head_dim <= 64 with more than 64 queries, else 4):
 //   for each 64-key tile t visible to the query tile:
-//     S = Q K_t^T                 16 scores per thread (4 rows x 4 keys)
+//     S = Q K_t^T                 RPT x 4 scores per thread (RPT rows x 4 keys)
 //     online softmax per row      row max / sum over the 16 threads of a half warp
-//     O += P V_t                  4 rows x D/16 columns per thread
+//     O += P V_t                  RPT rows x D/16 columns per thread
+// The dot products are bound by shared-memory bandwidth (each float4 read
+// feeds RPT or 4 FMAs), so the larger RPT of the head_dim-64 tile (8 rows per
+// K read) lifts the FMA rate; larger head dims keep RPT = 4 to fit the tile.
 // Rows are strided (row i of a thread is ty + 16*i, key j is tx + 16*j) so
 // that the shared-memory reads of K and V are conflict free with a +4 float
 // row pad.  Causal tiles above the diagonal are never loaded; CTAs are issued
@@ -23,12 +27,12 @@
 namespace wfattn {
 namespace {
 
-constexpr int kBM = 64;        // query rows per CTA
 constexpr int kBN = 64;        // keys per tile
 constexpr int kThreads = 256;  // 16 x 16
 
-template <int DP>
+template <int DP, int RPT>
 struct F32Layout {
+  static constexpr int kBM = 16 * RPT;   // query rows per CTA
   static constexpr int kLd = DP + 4;     // floats per Q/K/V smem row
   static constexpr int kPld = kBN + 16;  // floats per P smem row
   static constexpr size_t kFloats =
@@ -58,10 +62,11 @@ __device__ __forceinline__ void load_tile(float *__restrict__ dst, int ld,
   }
 }
 
-template <int DP>
+template <int DP, int RPT>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_f32_kernel(PrefillArgs a, float scale_log2, int64_t n_qtiles, int vec_in, int vec_out) {
-  using L = F32Layout<DP>;
+  using L = F32Layout<DP, RPT>;
+  constexpr int kBM = L::kBM;
   constexpr int kCpt = DP / 16;  // output columns per thread
   extern __shared__ __align__(16) float smem[];
   float *Qs = smem;
@@ -91,9 +96,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   load_tile<DP, kBM>(Qs, L::kLd, qp, a.qs.s, qrows, D, vec_in);
 
-  float m[4], l[4], acc[4][kCpt];
+  float m[RPT], l[RPT], acc[RPT][kCpt];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     m[i] = -INFINITY;
     l[i] = 0.f;
 #pragma unroll
@@ -108,35 +113,34 @@ __global__ void __launch_bounds__(kThreads, 2)
     load_tile<DP, kBN>(Vs, L::kLd, vp + n0 * a.vs.s, a.vs.s, krows, D, vec_in);
     __syncthreads();
 
-    float s[4][4];
+    float s[RPT][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
 
-#pragma unroll 4
+#pragma unroll 1
     for (int d4 = 0; d4 < d4n; ++d4) {
-      float4 qa[4], kb[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        qa[i] = *reinterpret_cast<const float4 *>(Qs + (ty + 16 * i) * L::kLd + d4 * 4);
+      float4 kb[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         kb[j] = *reinterpret_cast<const float4 *>(Ks + (tx + 16 * j) * L::kLd + d4 * 4);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RPT; ++i) {
+        const float4 qa = *reinterpret_cast<const float4 *>(Qs + (ty + 16 * i) * L::kLd + d4 * 4);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          s[i][j] = fmaf(qa[i].x, kb[j].x, s[i][j]);
-          s[i][j] = fmaf(qa[i].y, kb[j].y, s[i][j]);
-          s[i][j] = fmaf(qa[i].z, kb[j].z, s[i][j]);
-          s[i][j] = fmaf(qa[i].w, kb[j].w, s[i][j]);
+          s[i][j] = fmaf(qa.x, kb[j].x, s[i][j]);
+          s[i][j] = fmaf(qa.y, kb[j].y, s[i][j]);
+          s[i][j] = fmaf(qa.z, kb[j].z, s[i][j]);
+          s[i][j] = fmaf(qa.w, kb[j].w, s[i][j]);
         }
+      }
     }
 
     const bool need_mask = (n0 + kBN > a.Sk) || (a.causal && n0 + kBN - 1 > q0 + off);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPT; ++i) {
       const int64_t row = q0 + ty + 16 * i;
       float mx = -INFINITY;
 #pragma unroll
@@ -170,25 +174,49 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
 
     const int n4n = (krows + 3) / 4;
+    if constexpr (kCpt == 4) {
+      // head_dim <= 64: the four V rows of a key group first (16 registers),
+      // then one P float4 per row, so few values are live at once.
 #pragma unroll 2
-    for (int n4 = 0; n4 < n4n; ++n4) {
-      float4 pa[4];
+      for (int n4 = 0; n4 < n4n; ++n4) {
+        float4 vb[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        pa[i] = *reinterpret_cast<const float4 *>(Ps + (ty + 16 * i) * L::kPld + n4 * 4);
+        for (int u = 0; u < 4; ++u)
+          vb[u] = *reinterpret_cast<const float4 *>(Vs + (n4 * 4 + u) * L::kLd + tx * 4);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float *vrow = Vs + (n4 * 4 + u) * L::kLd;
+        for (int i = 0; i < RPT; ++i) {
+          const float4 pa = *reinterpret_cast<const float4 *>(Ps + (ty + 16 * i) * L::kPld + n4 * 4);
 #pragma unroll
-        for (int kk = 0; kk < kCpt / 4; ++kk) {
-          const float4 vb = *reinterpret_cast<const float4 *>(vrow + (tx + 16 * kk) * 4);
+          for (int u = 0; u < 4; ++u) {
+            const float p = u == 0 ? pa.x : u == 1 ? pa.y : u == 2 ? pa.z : pa.w;
+            acc[i][0] = fmaf(p, vb[u].x, acc[i][0]);
+            acc[i][1] = fmaf(p, vb[u].y, acc[i][1]);
+            acc[i][2] = fmaf(p, vb[u].z, acc[i][2]);
+            acc[i][3] = fmaf(p, vb[u].w, acc[i][3]);
+          }
+        }
+      }
+    } else {
+#pragma unroll 2
+      for (int n4 = 0; n4 < n4n; ++n4) {
+        float4 pa[RPT];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float p = u == 0 ? pa[i].x : u == 1 ? pa[i].y : u == 2 ? pa[i].z : pa[i].w;
-            acc[i][kk * 4 + 0] = fmaf(p, vb.x, acc[i][kk * 4 + 0]);
-            acc[i][kk * 4 + 1] = fmaf(p, vb.y, acc[i][kk * 4 + 1]);
-            acc[i][kk * 4 + 2] = fmaf(p, vb.z, acc[i][kk * 4 + 2]);
-            acc[i][kk * 4 + 3] = fmaf(p, vb.w, acc[i][kk * 4 + 3]);
+        for (int i = 0; i < RPT; ++i)
+          pa[i] = *reinterpret_cast<const float4 *>(Ps + (ty + 16 * i) * L::kPld + n4 * 4);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float *vrow = Vs + (n4 * 4 + u) * L::kLd;
+#pragma unroll
+          for (int kk = 0; kk < kCpt / 4; ++kk) {
+            const float4 vb = *reinterpret_cast<const float4 *>(vrow + (tx + 16 * kk) * 4);
+#pragma unroll
+            for (int i = 0; i < RPT; ++i) {
+              const float p = u == 0 ? pa[i].x : u == 1 ? pa[i].y : u == 2 ? pa[i].z : pa[i].w;
+              acc[i][kk * 4 + 0] = fmaf(p, vb.x, acc[i][kk * 4 + 0]);
+              acc[i][kk * 4 + 1] = fmaf(p, vb.y, acc[i][kk * 4 + 1]);
+              acc[i][kk * 4 + 2] = fmaf(p, vb.z, acc[i][kk * 4 + 2]);
+              acc[i][kk * 4 + 3] = fmaf(p, vb.w, acc[i][kk * 4 + 3]);
+            }
           }
         }
       }
@@ -196,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     const int r = ty + 16 * i;
     if (r >= qrows) continue;
     const float inv = 1.f / l[i];
@@ -219,14 +247,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-template <int DP>
+template <int DP, int RPT>
 cudaError_t launch_dp(const PrefillArgs &a, int device, cudaStream_t stream) {
-  using L = F32Layout<DP>;
+  using L = F32Layout<DP, RPT>;
   static_assert(L::kBytes <= 227 * 1024, "f32 tile does not fit in shared memory");
-  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_f32_kernel<DP>),
+  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_f32_kernel<DP, RPT>),
                                      (int)L::kBytes, device);
   if (err != cudaSuccess) return err;
-  const int64_t n_qtiles = (a.Sq + kBM - 1) / kBM;
+  const int64_t n_qtiles = (a.Sq + L::kBM - 1) / L::kBM;
   const int64_t blocks = n_qtiles * a.B * a.H;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
 
@@ -239,7 +267,7 @@ cudaError_t launch_dp(const PrefillArgs &a, int device, cudaStream_t stream) {
                        a.os.s % 4 == 0;
   const double log2e = 1.4426950408889634;
   const float scale_log2 = (float)((double)a.scale * log2e);
-  prefill_f32_kernel<DP><<<(unsigned)blocks, kThreads, L::kBytes, stream>>>(
+  prefill_f32_kernel<DP, RPT><<<(unsigned)blocks, kThreads, L::kBytes, stream>>>(
       a, scale_log2, n_qtiles, vec_in ? 1 : 0, vec_out ? 1 : 0);
   return cudaGetLastError();
 }
@@ -247,9 +275,12 @@ cudaError_t launch_dp(const PrefillArgs &a, int device, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
-  if (a.D <= 64) return launch_dp<64>(a, dev.device, stream);
-  if (a.D <= 128) return launch_dp<128>(a, dev.device, stream);
-  return launch_dp<256>(a, dev.device, stream);
+  // 128-row tiles for head_dim <= 64 unless the queries fit one 64-row tile
+  // (short sequences such as the per-token GPT-2 calls would be half padding).
+  if (a.D <= 64) return a.Sq > 64 ? launch_dp<64, 8>(a, dev.device, stream)
+                                  : launch_dp<64, 4>(a, dev.device, stream);
+  if (a.D <= 128) return launch_dp<128, 4>(a, dev.device, stream);
+  return launch_dp<256, 4>(a, dev.device, stream);
 }
 
 }  // namespace wfattn

@@ -425,6 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 17 : 11, k);
       const int64_t q_tile = it.q0 + t * kBM;
       const int64_t grow = q_tile + row;  // global query row
+      // Key tiles from j_mask on need masking: the ragged last tile (past Sk)
+      // and, when causal, the tiles that reach past the tile's first row.
+      int j_mask = (int)(p.Sk / kBN);
+      if (p.causal) j_mask = (int)imin64(j_mask, (q_tile + off + 1) / kBN);
+      const int64_t last_key = p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1;
       float m = -INFINITY;  // running offset of this row (log2 units)
       float l = 0.f;        // running sum of 2^(x - m)
       for (int j = 0; j < n; ++j, ++ns) {
@@ -432,10 +437,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         ptx::tc_fence_after();
         uint32_t sr[128];
-        const int64_t n0 = (int64_t)j * kBN;
-        const bool masked = (n0 + kBN > p.Sk) || (p.causal && n0 + kBN - 1 > q_tile + off);
-        const int64_t lim =
-            masked ? (p.causal ? imin64(grow + off, p.Sk - 1) : p.Sk - 1) - n0 : 127;
+        const bool masked = j >= j_mask;
+        // keys c > lim of this tile are masked (lim in [-1, 127] when masked)
+        const int lim = masked ? (int)imin64(last_key - (int64_t)j * kBN, 127) : 127;
         float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
         ptx::tmem_ld_32x32b_x64(lane_base + cS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
         ptx::tmem_wait_ld();

@@ -55,12 +55,17 @@ def _worker(rank, world, port, result_path, mode):
 
     q, k, v = _inputs()
     sp = ShardedPrefill(2, 6, 40, 16, dtype=torch.float32, device=torch.device("cpu"),
-                        compute=_oracle_compute)
+                        compute=_oracle_compute, chunks=1 if mode == "chunks1" else None)
     status = "ok"
     try:
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 fails before the collective")
-        out = sp(sp.shard(q), sp.shard(k), sp.shard(v))
+        if mode == "local":
+            # a rank-local [B, H/G, S, D] tensor of this rank's heads in chunk order
+            qs, ks, vs = (sp.split_local(torch.cat(sp.shard(t), dim=1)) for t in (q, k, v))
+            out = sp(qs, ks, vs)
+        else:
+            out = sp(sp.shard(q), sp.shard(k), sp.shard(v))
         np.save(f"{result_path}.{rank}.npy", out.contiguous().numpy())
     except RuntimeError as e:
         status = f"error: {e}"
@@ -100,6 +105,34 @@ def test_sharded_gather_matches_single_process(tmp_path):
         out = np.load(f"{path}.{r}.npy")
         assert out.shape == (2, 6, 40, 16)
         assert np.array_equal(out, ref)
+
+
+@pytest.mark.parametrize("mode", ["chunks1", "local"])
+def test_sharded_gather_one_chunk_and_rank_local_inputs(tmp_path, mode):
+    import oracle
+
+    path = _spawn(2, tmp_path, mode)
+    q, k, v = _inputs()
+    ref = oracle.attention(q.numpy(), k.numpy(), v.numpy())
+    for r in range(2):
+        assert open(f"{path}.{r}.status").read() == "ok"
+        assert np.array_equal(np.load(f"{path}.{r}.npy"), ref)
+
+
+def test_chunk_head_assignment_covers_every_head_once():
+    from warpforth_b200 import sharded
+
+    for heads, world in ((48, 8), (48, 4), (48, 2), (12, 3), (6, 2)):
+        chunks = sharded.default_chunks(heads, world)
+        seen = []
+        for c in range(chunks):
+            for rank in range(world):
+                sp = object.__new__(sharded.ShardedPrefill)  # rank's view, no process group
+                sp.H, sp.chunks, sp.rank, sp.ch = heads, chunks, rank, heads // world // chunks
+                lo, hi = sp.chunk_heads(c)
+                seen += list(range(lo, hi))
+        # gathered[c, rank, i] holds head chunk_heads(c)[0] + i: head-major order
+        assert seen == list(range(heads)), (heads, world, chunks)
 
 
 def test_single_rank_output_view_is_full_tensor():

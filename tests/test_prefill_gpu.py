@@ -171,6 +171,31 @@ def test_bf16_two_tile_kernel_strided_views(wf):
     assert _bf16_rel_err(out[:, :4], ref[:, :4]) <= BF16_REL_TOL
 
 
+def test_bf16_two_tile_kernel_graph_replays(wf):
+    # a captured launch of the persistent kernel replayed on new inputs must redo
+    # all the work each time
+    shape = (1, 160, 300, 64)
+    q, k, v = (torch.empty(shape, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    out = torch.empty_like(q)
+    wf.attention(q, k, v, out=out)  # first call outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        wf.attention(q, k, v, out=out)
+    for rep in range(3):
+        src = [_randn(shape, 480 + 3 * rep + i, torch.bfloat16) for i in range(3)]
+        for d, h in zip((q, k, v), src):
+            d.copy_(h)
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        o = out.float().cpu().numpy()
+        assert np.isfinite(o).all(), rep
+        ref = _oracle(*src, bh_range=(0, 2))
+        assert _bf16_rel_err(o[:, :2], ref[:, :2]) <= BF16_REL_TOL, rep
+    del graph
+
+
 def test_bf16_two_tile_kernel_noncausal_cross_lengths(wf):
     qq = _randn((2, 80, 130, 64), 460, torch.bfloat16)
     kk, vv = (_randn((2, 80, 333, 64), 461 + i, torch.bfloat16) for i in range(2))

@@ -676,7 +676,10 @@ def run_gpu(args, w: Workload) -> None:
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps * world * (2 if w.kind == "decode" else 1),
+            # kernels of this library per timed step, all ranks: decode = split + combine,
+            # sharded prefill = one launch per head chunk, otherwise one launch
+            "gpu_launches": args.steps * world * (2 if w.kind == "decode" else
+                                                  (sp.chunks if sp is not None else 1)),
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)

@@ -299,6 +299,9 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--shape", default=None,
                     help="B,H,S override of a prefill workload (profiling a smaller case)")
+    ap.add_argument("--transport", choices=["auto", "peer", "nccl"], default="auto",
+                    help="sharded prefill's gather: kernel stores into symmetric memory (peer) "
+                         "or chunked NCCL all-gathers")
     ap.add_argument("--chunks", type=int, default=0,
                     help="head chunks per rank for the sharded prefill's gather overlap "
                          "(0: the library default)")
@@ -506,15 +509,15 @@ def run_gpu(args, w: Workload) -> None:
         if w.sharded:
             q, k, v = (torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt) for _ in range(3))
             sp = ShardedPrefill(w.B, w.H, w.S, w.D, dtype=tdt, device=dev,
-                                chunks=args.chunks or None)
+                                chunks=args.chunks or None, transport=args.transport)
             qs, ks, vs = sp.shard(q), sp.shard(k), sp.shard(v)
             local_heads = sp.local_heads
             units = prefill_flops(w)  # whole job per step
             kernel_flops = prefill_flops(w, local_heads)
 
             def compute():
-                # this rank's heads chunk by chunk, each chunk's all-gather of O
-                # overlapping the next chunk's compute
+                # this rank's heads; the gather of O rides along (peer stores from
+                # the kernel, or per-chunk NCCL all-gathers overlapping compute)
                 sp(qs, ks, vs)
 
             def collective():
@@ -670,7 +673,8 @@ def run_gpu(args, w: Workload) -> None:
             "higher_is_better": hib,
             "scaling": "strong" if w.sharded else "weak",
             "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
-            "config": dict(config_of(w, world), device_timing=(
+            "config": dict(config_of(w, world), **({"gather": sp.transport} if sp else {}),
+                           device_timing=(
                 "per-rank CUDA events around each step" if w.sharded else
                 "CUDA events around each step's library call, replayed from a CUDA graph")),
             "roofline": roof,

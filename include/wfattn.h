@@ -106,6 +106,28 @@ WFATTN_API wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t head
                                const int64_t *o_strides, float scale, int causal, void *stream);
 
 /*
+ * bf16 prefill whose output is written to several buffers at once -- no
+ * counterpart in the reference, which runs on one GPU; this fuses the
+ * all-gather of a head-sharded multi-GPU prefill into the kernel.
+ *
+ * Same arguments as wfattn_prefill with dtype WFATTN_DTYPE_BF16, except that
+ * the output goes to every one of outputs[0 .. n_outputs-1] (1 <= n_outputs
+ * <= 8), each a [B, H, Sq, 64] bf16 view with the strides o_strides, e.g. this
+ * rank's heads inside every rank's full output buffer when the buffers are
+ * mapped across GPUs (peer or symmetric memory).  The kernel stores each
+ * finished output tile to all of them as it goes, so the transfer overlaps
+ * the computation.  The stores are complete when the kernel is; a caller that
+ * writes into other GPUs' buffers synchronises with those GPUs afterwards.
+ */
+WFATTN_API wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_q,
+                                                 int64_t seq_k, int64_t head_dim, const void *q,
+                                                 const int64_t *q_strides, const void *k,
+                                                 const int64_t *k_strides, const void *v,
+                                                 const int64_t *v_strides, void *const *outputs,
+                                                 int n_outputs, const int64_t *o_strides,
+                                                 float scale, int causal, void *stream);
+
+/*
  * Decode attention: one query token per (batch, head) against a padded KV
  * cache, split over key chunks and combined (split-KV).
  *

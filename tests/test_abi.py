@@ -56,6 +56,22 @@ def test_prefill_rejects_bad_arguments_on_host(kw):
     assert lib.wfattn_last_error()
 
 
+def test_prefill_gather_rejects_bad_arguments_on_host():
+    lib = _lib.load()
+    outs = (ctypes.c_void_p * 9)(*([16] * 9))
+
+    def call(outputs, n, q=16, sq=4, sk=4):
+        return lib.wfattn_prefill_gather(1, 1, sq, sk, 64, q, None, 16, None, 16, None,
+                                         outputs, n, None, 0.0, 1, None)
+
+    assert call(outs, 0) == _lib.INVALID_ARG
+    assert call(outs, 9) == _lib.INVALID_ARG  # at most 8 destinations
+    assert call(None, 2) == _lib.INVALID_ARG
+    assert call(outs, 2, q=None) == _lib.INVALID_ARG
+    assert call(outs, 2, sq=5, sk=4) == _lib.INVALID_ARG  # causal needs seq_k >= seq_q
+    assert lib.wfattn_last_error()
+
+
 def test_reference_abi_rejects_foreign_geometry_on_host():
     lib = _lib.load()
     bad = _lib.Dim3(3, 1, 1)

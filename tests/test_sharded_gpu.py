@@ -1,0 +1,73 @@
+"""Head-sharded prefill on 2 GPUs: both transports against one-GPU results.
+
+peer: every rank's kernel stores its heads into every rank's symmetric output
+buffer over NVLink (wfattn_prefill_gather); the gathered output must be
+bit-identical to the same kernel run for all heads on one GPU.  nccl: chunked
+all-gathers of per-rank outputs; within the bf16 tolerance of that result.
+Skipped on boxes with fewer than two GPUs.
+"""
+
+from __future__ import annotations
+
+import socket
+import sys
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, path):
+    sys.path.insert(0, str(ROOT))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    from warpforth_b200 import warpforth as wf
+    from warpforth_b200.sharded import ShardedPrefill
+
+    b, h, s, d = 2, 16, 640, 64
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(b, h, s, d, generator=g).bfloat16().to(dev) for _ in range(3))
+    ref = torch.empty_like(q)
+    wf.attention_gather(q, k, v, [ref])  # the two-tile kernel for every head, one GPU
+    res = {}
+    for transport in ("peer", "nccl"):
+        sp = ShardedPrefill(b, h, s, d, dtype=torch.bfloat16, device=dev, transport=transport)
+        for _ in range(2):  # the second step reuses the buffers
+            out = sp(sp.shard(q), sp.shard(k), sp.shard(v))
+        torch.cuda.synchronize()
+        o = out.float()
+        res[transport] = (sp.transport, bool(torch.equal(out.contiguous(), ref)),
+                          float((o - ref.float()).abs().max() / ref.float().abs().max()))
+    np.save(f"{path}.{rank}.npy", np.array([res["peer"][1], res["nccl"][2],
+                                             res["peer"][0] == "peer"], dtype=np.float64))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gpu_peer_and_nccl_transports(tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path = str(tmp_path / "res")
+    mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        peer_exact, nccl_rel, used_peer = np.load(f"{path}.{r}.npy")
+        assert used_peer == 1.0
+        assert peer_exact == 1.0
+        assert nccl_rel <= 2e-2

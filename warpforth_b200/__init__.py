@@ -11,7 +11,7 @@ this package holds the Python side of the drop-in boundary:
 
 from __future__ import annotations
 
-__all__ = ["AttentionKernel", "attention", "decode", "DecodeWorkspace"]
+__all__ = ["AttentionKernel", "attention", "attention_gather", "decode", "DecodeWorkspace"]
 
 
 def __getattr__(name):  # lazy: importing the package does not import torch

@@ -92,6 +92,13 @@ struct Params {
   unsigned int *status;
 };
 
+// Output tensor maps: the output buffer, or one per GPU that receives a copy
+// (the all-gather of a head-sharded prefill done by the kernel's own stores).
+struct OutMaps {
+  CUtensorMap m[kMaxOutputPeers];
+  int n;
+};
+
 // One work item: 256 query rows (tiles A and B) of one (batch, head).
 struct Item {
   int b, h;
@@ -180,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_bf16_2q_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v,
-                           const __grid_constant__ CUtensorMap tm_o, const Params p) {
+                           const __grid_constant__ OutMaps outs, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~uintptr_t(1023));
@@ -222,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == kTmaVWarp && lane == 0) {
     ptx::prefetch_tmap(&tm_v);
-    ptx::prefetch_tmap(&tm_o);
+    for (int r = 0; r < outs.n; ++r) ptx::prefetch_tmap(&outs.m[r]);
   }
   if (warp == kMmaQkWarp) {
     if (lane == 0) trace(1, 1);
@@ -570,8 +577,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        ptx::tma_store_4d(&tm_o, ptx::smem_u32(stage), 0, (int)(q_tile + 32 * (warp & 3)), it.h,
-                          it.b);
+        // one store per destination (other GPUs' buffers over NVLink), all
+        // reading the same slab; they complete as one bulk group
+        for (int r = 0; r < outs.n; ++r)
+          ptx::tma_store_4d(&outs.m[r], ptx::smem_u32(stage), 0, (int)(q_tile + 32 * (warp & 3)),
+                            it.h, it.b);
         ptx::bulk_commit_group();
       }
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 15 : 9, k);
@@ -609,12 +619,18 @@ cudaError_t set_trace_prefill_2q(void *p) { return set_trace_symbol(p); }
 cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
                                    cudaStream_t stream) {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-  CUtensorMap tq, tk, tv, to;
+  CUtensorMap tq, tk, tv;
   if (!make_bf16_map_64x128(&tq, a.q, a.B, a.H, a.Sq, a.qs) ||
       !make_bf16_map_64x128(&tk, a.k, a.B, a.H, a.Sk, a.ks) ||
-      !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs) ||
-      !make_bf16_map_64xR(&to, a.o, a.B, a.H, a.Sq, a.os, 32))
+      !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
     return cudaErrorInvalidValue;
+  OutMaps outs;
+  outs.n = a.n_peers > 0 ? a.n_peers : 1;
+  if (outs.n > kMaxOutputPeers) return cudaErrorInvalidValue;
+  for (int r = 0; r < outs.n; ++r)
+    if (!make_bf16_map_64xR(&outs.m[r], a.n_peers > 0 ? a.o_peers[r] : a.o, a.B, a.H, a.Sq, a.os,
+                            32))
+      return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
     return cudaErrorInvalidValue;
   cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_bf16_2q_kernel),
@@ -637,7 +653,7 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   if (p.n_items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   // Persistent: one CTA per SM walks the items (fewer CTAs for small problems).
   const int64_t blocks = p.n_items < dev.sm_count ? p.n_items : dev.sm_count;
-  prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, outs, p);
   return cudaGetLastError();
 }
 

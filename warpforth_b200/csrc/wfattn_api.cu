@@ -85,6 +85,30 @@ float resolve_scale(float scale, int64_t D) {
   return scale > 0.f ? scale : (float)(1.0 / sqrt((double)D));
 }
 
+// Layout rules of the bf16 tensor-core kernels (TMA tensor maps).
+wfattn_status_t check_bf16(const PrefillArgs &a) {
+  if (a.D != 64) return fail(WFATTN_UNSUPPORTED, "bf16 path supports head_dim == 64 only");
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(a.q) || !al16(a.k) || !al16(a.v) || (a.o && !al16(a.o)))
+    return fail(WFATTN_INVALID_ARG, "bf16 tensors must be 16-byte aligned");
+  for (int r = 0; r < a.n_peers; ++r)
+    if (!a.o_peers[r] || !al16(a.o_peers[r]))
+      return fail(WFATTN_INVALID_ARG, "output %d is null or not 16-byte aligned", r);
+  const Strides3 *all[4] = {&a.qs, &a.ks, &a.vs, &a.os};
+  for (const Strides3 *x : all)
+    if (x->b % 8 || x->h % 8 || x->s % 8)
+      return fail(WFATTN_INVALID_ARG, "bf16 strides must be multiples of 8 elements");
+  const int64_t ext_q[3] = {a.B, a.H, a.Sq}, ext_k[3] = {a.B, a.H, a.Sk};
+  for (int i = 0; i < 3; ++i) {
+    const int64_t sq[3] = {a.qs.b, a.qs.h, a.qs.s}, sk[3] = {a.ks.b, a.ks.h, a.ks.s},
+                  sv[3] = {a.vs.b, a.vs.h, a.vs.s}, so[3] = {a.os.b, a.os.h, a.os.s};
+    if ((ext_q[i] > 1 && (sq[i] == 0 || so[i] == 0)) ||
+        (ext_k[i] > 1 && (sk[i] == 0 || sv[i] == 0)))
+      return fail(WFATTN_INVALID_ARG, "bf16 path does not take zero (broadcast) strides");
+  }
+  return WFATTN_OK;
+}
+
 }  // namespace
 
 namespace {
@@ -131,13 +155,17 @@ const char *wfattn_status_string(wfattn_status_t status) {
 
 const char *wfattn_last_error(void) { return t_last_error.c_str(); }
 
-wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t seq_q,
-                               int64_t seq_k, int64_t head_dim, const void *q,
-                               const int64_t *q_strides, const void *k, const int64_t *k_strides,
-                               const void *v, const int64_t *v_strides, void *o,
-                               const int64_t *o_strides, float scale, int causal, void *stream) {
-  t_last_error.clear();
-  if (!q || !k || !v || !o) return fail(WFATTN_INVALID_ARG, "null tensor pointer");
+}  // extern "C"
+
+namespace {
+
+// Argument checks and setup shared by the prefill entry points.
+wfattn_status_t prepare_prefill(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                                int64_t head_dim, const void *q, const int64_t *q_strides,
+                                const void *k, const int64_t *k_strides, const void *v,
+                                const int64_t *v_strides, void *o, const int64_t *o_strides,
+                                float scale, int causal, PrefillArgs *a, DeviceInfo *dev) {
+  if (!q || !k || !v) return fail(WFATTN_INVALID_ARG, "null tensor pointer");
   if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 || head_dim < 1)
     return fail(WFATTN_INVALID_ARG, "sizes must be >= 1 (B=%lld H=%lld Sq=%lld Sk=%lld D=%lld)",
                 (long long)batch, (long long)heads, (long long)seq_q, (long long)seq_k,
@@ -146,31 +174,48 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
     return fail(WFATTN_INVALID_ARG, "causal attention needs seq_k >= seq_q (%lld < %lld)",
                 (long long)seq_k, (long long)seq_q);
   if (!(scale == scale)) return fail(WFATTN_INVALID_ARG, "scale is NaN");
-  PrefillArgs a;
-  a.B = batch;
-  a.H = heads;
-  a.Sq = seq_q;
-  a.Sk = seq_k;
-  a.D = head_dim;
-  a.q = q;
-  a.k = k;
-  a.v = v;
-  a.o = o;
-  a.qs = resolve_strides(q_strides, heads, seq_q, head_dim);
-  a.ks = resolve_strides(k_strides, heads, seq_k, head_dim);
-  a.vs = resolve_strides(v_strides, heads, seq_k, head_dim);
-  a.os = resolve_strides(o_strides, heads, seq_q, head_dim);
-  if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os))
+  a->B = batch;
+  a->H = heads;
+  a->Sq = seq_q;
+  a->Sk = seq_k;
+  a->D = head_dim;
+  a->q = q;
+  a->k = k;
+  a->v = v;
+  a->o = o;
+  a->qs = resolve_strides(q_strides, heads, seq_q, head_dim);
+  a->ks = resolve_strides(k_strides, heads, seq_k, head_dim);
+  a->vs = resolve_strides(v_strides, heads, seq_k, head_dim);
+  a->os = resolve_strides(o_strides, heads, seq_q, head_dim);
+  if (!strides_ok(a->qs) || !strides_ok(a->ks) || !strides_ok(a->vs) || !strides_ok(a->os))
     return fail(WFATTN_INVALID_ARG, "negative stride");
-  a.scale = resolve_scale(scale, head_dim);
-  a.causal = causal ? 1 : 0;
-
-  DeviceInfo dev;
-  wfattn_status_t st = current_device(&dev);
+  a->scale = resolve_scale(scale, head_dim);
+  a->causal = causal ? 1 : 0;
+  wfattn_status_t st = current_device(dev);
   if (st != WFATTN_OK) return st;
-  if (!is_sm100(dev))
+  if (!is_sm100(*dev))
     return fail(WFATTN_UNSUPPORTED, "libwfattn is built for sm_100a; device %d is sm_%d%d",
-                dev.device, dev.cc_major, dev.cc_minor);
+                dev->device, dev->cc_major, dev->cc_minor);
+  return WFATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t seq_q,
+                               int64_t seq_k, int64_t head_dim, const void *q,
+                               const int64_t *q_strides, const void *k, const int64_t *k_strides,
+                               const void *v, const int64_t *v_strides, void *o,
+                               const int64_t *o_strides, float scale, int causal, void *stream) {
+  t_last_error.clear();
+  if (!o) return fail(WFATTN_INVALID_ARG, "null tensor pointer");
+  PrefillArgs a;
+  DeviceInfo dev;
+  wfattn_status_t st = prepare_prefill(batch, heads, seq_q, seq_k, head_dim, q, q_strides, k,
+                                       k_strides, v, v_strides, o, o_strides, scale, causal, &a,
+                                       &dev);
+  if (st != WFATTN_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err;
   if (dtype == WFATTN_DTYPE_F32) {
@@ -180,22 +225,8 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
     return WFATTN_OK;
   }
   if (dtype == WFATTN_DTYPE_BF16) {
-    if (head_dim != 64) return fail(WFATTN_UNSUPPORTED, "bf16 path supports head_dim == 64 only");
-    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    if (!al16(q) || !al16(k) || !al16(v) || !al16(o))
-      return fail(WFATTN_INVALID_ARG, "bf16 tensors must be 16-byte aligned");
-    const Strides3 *all[4] = {&a.qs, &a.ks, &a.vs, &a.os};
-    for (const Strides3 *x : all)
-      if (x->b % 8 || x->h % 8 || x->s % 8)
-        return fail(WFATTN_INVALID_ARG, "bf16 strides must be multiples of 8 elements");
-    const int64_t ext_q[3] = {batch, heads, seq_q}, ext_k[3] = {batch, heads, seq_k};
-    for (int i = 0; i < 3; ++i) {
-      const int64_t sq[3] = {a.qs.b, a.qs.h, a.qs.s}, sk[3] = {a.ks.b, a.ks.h, a.ks.s},
-                    sv[3] = {a.vs.b, a.vs.h, a.vs.s}, so[3] = {a.os.b, a.os.h, a.os.s};
-      if ((ext_q[i] > 1 && (sq[i] == 0 || so[i] == 0)) ||
-          (ext_k[i] > 1 && (sk[i] == 0 || sv[i] == 0)))
-        return fail(WFATTN_INVALID_ARG, "bf16 path does not take zero (broadcast) strides");
-    }
+    st = check_bf16(a);
+    if (st != WFATTN_OK) return st;
     // Two 128-row query tiles per CTA (one CTA per SM) halve the K/V traffic
     // per FLOP; when that grid would not even give every SM a CTA, one tile
     // per CTA (two CTAs per SM) spreads the few rows over twice the SMs and
@@ -207,6 +238,31 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
     return WFATTN_OK;
   }
   return fail(WFATTN_INVALID_ARG, "unknown dtype %d", dtype);
+}
+
+wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                                      int64_t head_dim, const void *q, const int64_t *q_strides,
+                                      const void *k, const int64_t *k_strides, const void *v,
+                                      const int64_t *v_strides, void *const *outputs,
+                                      int n_outputs, const int64_t *o_strides, float scale,
+                                      int causal, void *stream) {
+  t_last_error.clear();
+  if (!outputs || n_outputs < 1 || n_outputs > kMaxOutputPeers)
+    return fail(WFATTN_INVALID_ARG, "n_outputs must be in [1, %d] with an output array",
+                kMaxOutputPeers);
+  PrefillArgs a;
+  DeviceInfo dev;
+  wfattn_status_t st = prepare_prefill(batch, heads, seq_q, seq_k, head_dim, q, q_strides, k,
+                                       k_strides, v, v_strides, nullptr, o_strides, scale,
+                                       causal, &a, &dev);
+  if (st != WFATTN_OK) return st;
+  a.o_peers = outputs;
+  a.n_peers = n_outputs;
+  st = check_bf16(a);
+  if (st != WFATTN_OK) return st;
+  const cudaError_t err = launch_prefill_bf16_2q(a, dev, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
+  return WFATTN_OK;
 }
 
 wfattn_status_t wfattn_attention(const float *Q, const float *K, const float *V, float *O,

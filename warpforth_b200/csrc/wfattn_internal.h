@@ -21,6 +21,8 @@ struct Strides3 {
   int64_t b, h, s;
 };
 
+constexpr int kMaxOutputPeers = 8;
+
 struct PrefillArgs {
   int64_t B, H, Sq, Sk, D;
   const void *q, *k, *v;
@@ -28,6 +30,10 @@ struct PrefillArgs {
   Strides3 qs, ks, vs, os;
   float scale;  // already resolved (> 0)
   int causal;
+  // bf16 two-tile kernel only: when n_peers > 0 the output goes to every one of
+  // these buffers (same shape and strides os, possibly on other GPUs) instead of o.
+  void *const *o_peers = nullptr;
+  int n_peers = 0;
 };
 
 struct DecodeArgs {

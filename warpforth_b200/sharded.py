@@ -2,22 +2,28 @@
 
 Every (batch, head) pair of attention is independent, so G ranks (one process
 per GPU) split the heads evenly and compute them with no exchange; the only
-collective is the all-gather of O.  To hide that gather behind compute, the
-heads are cut into C chunks of H/C heads, each chunk split evenly over the
-ranks: rank r owns heads [c*H/C + r*h, c*H/C + (r+1)*h) of chunk c, with
-h = H/(C*G).  A rank computes its part of chunk c, then starts the all-gather
-of chunk c (asynchronously, on the collective's own stream) while it computes
-chunk c+1.
+exchange is the all-gather of O.  Two transports:
 
-Each rank writes its heads into its slot of a head-major buffer
-[C, G, h, B, S, D]; the gathers run in place, and the buffer is exactly a
-strided [B, H, S, D] view (no copy):
+* ``peer`` (bf16 on GPUs, the default there): every rank's full [B, H, S, D]
+  output lives in symmetric memory mapped on all ranks.  The attention kernel
+  stores each finished output tile of its heads into every rank's buffer over
+  NVLink (``wfattn_prefill_gather``), so the gather rides along tile by tile
+  with the compute; one cross-rank barrier ends the step.  Rank r owns heads
+  [r*H/G, (r+1)*H/G).
+* ``nccl`` (any dtype or device, and the fallback): the heads are cut into C
+  chunks of H/C heads, each chunk split evenly over the ranks: rank r owns
+  heads [c*H/C + r*h, c*H/C + (r+1)*h) of chunk c, with h = H/(C*G).  A rank
+  computes its part of chunk c, then starts the all-gather of chunk c
+  (asynchronously, on the collective's own stream) while it computes chunk
+  c+1.  Each rank writes its heads into its slot of a head-major buffer
+  [C, G, h, B, S, D]; the gathers run in place, and the buffer is exactly a
+  strided [B, H, S, D] view (no copy):
 
-    gathered.view(H, B, S, D).permute(1, 0, 2, 3)  ->  [B, H, S, D]
+      gathered.view(H, B, S, D).permute(1, 0, 2, 3)  ->  [B, H, S, D]
 
-The collective goes through ``torch.distributed`` (NCCL over NVLink on GPUs,
-gloo on CPU for the tests).  The per-rank compute is injectable so that the
-shard/gather logic can be tested on CPU ranks against the oracle.
+The NCCL transport goes through ``torch.distributed`` (gloo on CPU for the
+tests); its per-rank compute is injectable so that the shard/gather logic can
+be tested on CPU ranks against the oracle.
 """
 
 from __future__ import annotations
@@ -59,28 +65,62 @@ def _default_compute(q, k, v, *, causal, scale, out):
 class ShardedPrefill:
     """Runs this rank's share of a [B, H, S, D] attention and all-gathers O.
 
-    ``gathered`` ([C, G, h, B, S, D]) is allocated once and reused.  ``__call__``
+    The output buffer (``full`` for the peer transport, ``gathered`` =
+    [C, G, h, B, S, D] for NCCL) is allocated once and reused.  ``__call__``
     takes this rank's q/k/v as per-chunk lists of [B, h, S, D] views (from
-    ``shard`` of the full tensors or ``split_local`` of a rank-local tensor)
-    and returns the full output as a [B, H, S, D] view of ``gathered``.
+    ``shard`` of the full tensors or ``split_local`` of a rank-local tensor;
+    one chunk with the peer transport) and returns the full [B, H, S, D]
+    output.  ``transport`` is "auto" (peer where possible), "peer" or "nccl".
     """
 
     def __init__(self, batch: int, heads: int, seq: int, head_dim: int, *,
                  dtype: torch.dtype, device: torch.device, group=None,
-                 compute: ComputeFn | None = None, chunks: int | None = None) -> None:
+                 compute: ComputeFn | None = None, chunks: int | None = None,
+                 transport: str = "auto") -> None:
+        if transport not in ("auto", "peer", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         head_range(heads, self.world, self.rank)  # validates the even split
         self.local_heads = heads // self.world
+        self.B, self.H, self.S, self.D = batch, heads, seq, head_dim
+        self.transport = "nccl"
+        peer_ok = (self.world > 1 and torch.device(device).type == "cuda"
+                   and dtype == torch.bfloat16 and head_dim == 64 and compute is None
+                   and chunks in (None, 1))
+        if transport == "peer" and not peer_ok:
+            raise ValueError("the peer transport needs bf16, head_dim 64, CUDA and >1 rank")
+        if transport in ("auto", "peer") and peer_ok:
+            try:
+                self._setup_peer(dtype, device)
+                self.transport = "peer"
+            except Exception:
+                if transport == "peer":
+                    raise
+        if self.transport == "peer":
+            self.chunks, self.ch = 1, self.local_heads
+            return
         self.chunks = chunks or default_chunks(heads, self.world)
         if self.local_heads % self.chunks:
             raise ValueError(f"{self.local_heads} heads per rank cannot form {self.chunks} chunks")
         self.ch = self.local_heads // self.chunks
-        self.B, self.H, self.S, self.D = batch, heads, seq, head_dim
         self.gathered = torch.empty((self.chunks, self.world, self.ch, batch, seq, head_dim),
                                     dtype=dtype, device=device)
         self.compute = compute or _default_compute
+
+    def _setup_peer(self, dtype, device) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        group_name = (self.group or dist.group.WORLD).group_name
+        shape = (self.B, self.H, self.S, self.D)
+        self.full = symm_mem.empty(shape, dtype=dtype, device=device)
+        self.hdl = symm_mem.rendezvous(self.full, group_name)
+        h0 = self.rank * self.local_heads
+        # this rank's heads inside every rank's output buffer (peer mappings)
+        self.peer_outs = [self.hdl.get_remote_tensor(r, shape, dtype)[:, h0:h0 + self.local_heads]
+                          for r in range(self.world)]
+        self._sync = torch.zeros(1, dtype=torch.int32, device=device)
 
     def chunk_heads(self, c: int) -> tuple[int, int]:
         """Global head range of this rank's part of chunk c."""
@@ -97,6 +137,8 @@ class ShardedPrefill:
         return [t[:, c * self.ch:(c + 1) * self.ch] for c in range(self.chunks)]
 
     def output_view(self) -> torch.Tensor:
+        if self.transport == "peer":
+            return self.full
         return self.gathered.view(self.H, self.B, self.S, self.D).permute(1, 0, 2, 3)
 
     def _compute_chunk(self, c, q, k, v, causal, scale):
@@ -107,13 +149,27 @@ class ShardedPrefill:
     def compute_local(self, qs: Sequence[torch.Tensor], ks: Sequence[torch.Tensor],
                       vs: Sequence[torch.Tensor], *, causal: bool = True,
                       scale: float | None = None) -> None:
-        """This rank's heads only, no collective."""
+        """This rank's heads only, without the final synchronisation (peer transport: the
+        kernel still stores into every rank's buffer)."""
+        if self.transport == "peer":
+            from .warpforth import attention_gather
+
+            attention_gather(qs[0], ks[0], vs[0], self.peer_outs, causal=causal, scale=scale)
+            return
         for c in range(self.chunks):
             self._compute_chunk(c, qs[c], ks[c], vs[c], causal, scale)
 
     def __call__(self, qs: Sequence[torch.Tensor], ks: Sequence[torch.Tensor],
                  vs: Sequence[torch.Tensor], *, causal: bool = True,
                  scale: float | None = None) -> torch.Tensor:
+        if self.transport == "peer":
+            self.compute_local(qs, ks, vs, causal=causal, scale=scale)
+            # A one-element NCCL all-reduce as the cross-rank barrier: once it is
+            # done on this rank, every rank's attention kernel (queued before its
+            # all-reduce) has completed its stores into this rank's buffer.  It is
+            # bounded by the process group's timeout.
+            dist.all_reduce(self._sync, group=self.group)
+            return self.full
         works = []
         for c in range(self.chunks):
             self._compute_chunk(c, qs[c], ks[c], vs[c], causal, scale)

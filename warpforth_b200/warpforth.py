@@ -105,6 +105,37 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool
     return out
 
 
+def attention_gather(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     outs: list[torch.Tensor], *, causal: bool = True,
+                     scale: float | None = None) -> None:
+    """bf16 attention of q/k/v ([B, H, S, 64] CUDA views) written to every tensor in ``outs``.
+
+    Each ``outs[i]`` is a [B, H, Sq, 64] bf16 view with the same strides, possibly of another
+    GPU's memory (a peer mapping of a symmetric buffer): the kernel stores every finished
+    output tile to all of them, so a head-sharded prefill needs no separate all-gather.  The
+    caller synchronises with the other GPUs after the call.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t)
+        if t.dtype != torch.bfloat16 or t.dim() != 4 or t.stride(3) != 1:
+            raise ValueError(f"{name} must be a bf16 [B, H, S, D] view with a unit last stride")
+    b, h, sq, d = q.shape
+    sk = k.shape[2]
+    if k.shape != (b, h, sk, d) or v.shape != (b, h, sk, d):
+        raise ValueError("shape mismatch")
+    if not 1 <= len(outs) <= 8:
+        raise ValueError("outs must hold 1 to 8 tensors")
+    for o in outs:
+        if o.shape != q.shape or o.dtype != q.dtype or o.stride() != outs[0].stride():
+            raise ValueError("every output must match q's shape and dtype with one set of strides")
+    lib = _lib.load()
+    st = [_lib.strides_arg(t.stride()[:3]) for t in (q, k, v, outs[0])]
+    ptrs = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+    _lib.check(lib.wfattn_prefill_gather(
+        b, h, sq, sk, d, _ptr(q), st[0], _ptr(k), st[1], _ptr(v), st[2], ptrs, len(outs), st[3],
+        float(scale) if scale else 0.0, 1 if causal else 0, _stream_handle(q.device)))
+
+
 class DecodeWorkspace:
     """Caller-owned scratch for ``decode`` (grown on demand, reused across calls)."""
 

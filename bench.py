@@ -300,8 +300,8 @@ def main() -> None:
     ap.add_argument("--shape", default=None,
                     help="B,H,S override of a prefill workload (profiling a smaller case)")
     ap.add_argument("--transport", choices=["auto", "peer", "nccl"], default="auto",
-                    help="sharded prefill's gather: kernel stores into symmetric memory (peer) "
-                         "or chunked NCCL all-gathers")
+                    help="sharded prefill's gather: the kernel stores into every rank's buffer "
+                         "over CUDA IPC mappings (peer) or chunked NCCL all-gathers")
     ap.add_argument("--chunks", type=int, default=0,
                     help="head chunks per rank for the sharded prefill's gather overlap "
                          "(0: the library default)")
@@ -687,6 +687,8 @@ def run_gpu(args, w: Workload) -> None:
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
+    if sp is not None:
+        sp.close()  # collective: unmaps and frees the peer output buffers
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

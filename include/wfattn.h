@@ -5,8 +5,9 @@
  *
  * Conventions shared by every entry point:
  *  - All tensor pointers are DEVICE pointers owned by the caller.  The library
- *    never allocates device memory on these paths; outputs are fully
- *    overwritten over their logical extent.
+ *    never allocates device memory on the attention paths (wfattn_peer_alloc
+ *    allocates on request); outputs are fully overwritten over their logical
+ *    extent.
  *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream,
  *    which is what the reference launches on: warpforth-runner.cpp:318-319).
  *    Every call is asynchronous with respect to the host, like the reference's
@@ -114,9 +115,9 @@ WFATTN_API wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t head
  * the output goes to every one of outputs[0 .. n_outputs-1] (1 <= n_outputs
  * <= 8), each a [B, H, Sq, 64] bf16 view with the strides o_strides, e.g. this
  * rank's heads inside every rank's full output buffer when the buffers are
- * mapped across GPUs (peer or symmetric memory).  The kernel stores each
- * finished output tile to all of them as it goes, so the transfer overlaps
- * the computation.  The stores are complete when the kernel is; a caller that
+ * mapped across GPUs (wfattn_peer_alloc / wfattn_peer_open).  The kernel
+ * stores each finished output tile to all of them as it goes, so the transfer
+ * overlaps the computation.  The stores are complete when the kernel is; a caller that
  * writes into other GPUs' buffers synchronises with those GPUs afterwards.
  */
 WFATTN_API wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_q,
@@ -185,6 +186,36 @@ WFATTN_API wfattn_status_t wfattn_decode_noalloc(int64_t batch, int64_t heads, i
                                                  const int32_t *kv_lens, float *o,
                                                  const int64_t *o_strides, float scale,
                                                  void *stream);
+
+/*
+ * Peer buffers -- no counterpart in the reference, which runs on one GPU.
+ *
+ * Device memory that other processes on the node can map, for the outputs of
+ * a head-sharded prefill (wfattn_prefill_gather): every rank allocates its
+ * full output buffer with wfattn_peer_alloc, sends the 64-byte handle to the
+ * other ranks (any host channel), and maps theirs with wfattn_peer_open; the
+ * kernel then stores straight into the mapped buffers over NVLink.  Plain
+ * CUDA IPC: cudaMalloc'd memory, ordinary peer mappings, no multicast.
+ *
+ * wfattn_peer_alloc:  `bytes` of device memory on `device` and its handle.
+ * wfattn_peer_open:   maps another process's buffer on `device` (never one's
+ *                     own handle).
+ * wfattn_peer_close:  unmaps a buffer returned by wfattn_peer_open.
+ * wfattn_peer_free:   frees a buffer from wfattn_peer_alloc; every process
+ *                     that mapped it closes its mapping first.
+ * These calls synchronise as cudaMalloc / cudaFree do; the current device is
+ * left as it was.
+ */
+typedef struct wfattn_peer_handle {
+  unsigned char bytes[64];
+} wfattn_peer_handle_t;
+
+WFATTN_API wfattn_status_t wfattn_peer_alloc(size_t bytes, int device, void **ptr,
+                                             wfattn_peer_handle_t *handle);
+WFATTN_API wfattn_status_t wfattn_peer_open(const wfattn_peer_handle_t *handle, int device,
+                                            void **ptr);
+WFATTN_API wfattn_status_t wfattn_peer_close(void *ptr, int device);
+WFATTN_API wfattn_status_t wfattn_peer_free(void *ptr, int device);
 
 /*
  * Reads (and optionally clears) the device-side status word of the current

@@ -154,3 +154,85 @@ def test_failed_rank_surfaces_as_collective_error(tmp_path):
     assert open(f"{path}.1.status").read().startswith("error: rank 1 fails")
     st0 = open(f"{path}.0.status").read()
     assert st0.startswith("error:"), st0
+
+
+class _FakePeerLib:
+    """Stands in for libwfattn's peer-buffer calls on a CPU rank: allocation and mapping
+    succeed or fail as told, and every call is recorded."""
+
+    def __init__(self, alloc_ok: bool, open_ok: bool) -> None:
+        self.alloc_ok, self.open_ok, self.calls = alloc_ok, open_ok, []
+
+    def wfattn_peer_alloc(self, nbytes, device, ptr, handle):
+        self.calls.append("alloc")
+        if not self.alloc_ok:
+            return 3
+        ptr._obj.value = 1 << 20
+        handle._obj.bytes[0] = 7
+        return 0
+
+    def wfattn_peer_open(self, handle, device, ptr):
+        self.calls.append("open")
+        if not self.open_ok:
+            return 3
+        ptr._obj.value = 2 << 20
+        return 0
+
+    def wfattn_peer_close(self, ptr, device):
+        self.calls.append("close")
+        return 0
+
+    def wfattn_peer_free(self, ptr, device):
+        self.calls.append("free")
+        return 0
+
+
+def _peer_worker(rank, world, port, result_path, case):
+    import types
+
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=10))
+    from warpforth_b200 import _lib, peer
+
+    alloc_ok = not (case == "alloc" and rank == 0)
+    open_ok = not (case == "open" and rank == 1)
+    fake = _FakePeerLib(alloc_ok, open_ok)
+
+    def check(status):
+        if status:
+            raise _lib.WfattnError(status, "fake failure")
+
+    peer._lib = types.SimpleNamespace(load=lambda: fake, check=check, PeerHandle=_lib.PeerHandle,
+                                      WfattnError=_lib.WfattnError)
+    try:
+        peer.PeerBuffer((2, 4, 8, 64), torch.bfloat16, torch.device("cuda", rank))
+        status = "no error"
+    except peer.PeerSetupError as e:
+        status = f"PeerSetupError: {e}"
+    with open(f"{result_path}.{rank}.status", "w") as f:
+        f.write(status + "\n" + ",".join(fake.calls))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["alloc", "open"])
+def test_peer_buffer_setup_failure_is_raised_on_every_rank(tmp_path, case):
+    """One rank's failed allocation (rank 0) or mapping (rank 1) makes every rank raise
+    PeerSetupError after releasing what it set up, so all ranks can fall back together."""
+    port = _free_port()
+    path = str(tmp_path / "res")
+    mp.start_processes(_peer_worker, args=(2, port, path, case), nprocs=2, join=True,
+                       start_method="spawn")
+    out = {r: open(f"{path}.{r}.status").read().split("\n") for r in range(2)}
+    for r in range(2):
+        assert out[r][0].startswith("PeerSetupError: rank "), out[r]
+    if case == "alloc":
+        assert out[0][1] == "alloc"  # nothing to release
+        assert out[1][1] == "alloc,free"  # never maps, frees its own buffer
+        assert "rank 0" in out[1][0]
+    else:
+        assert out[0][1] == "alloc,open,close,free"  # unmaps rank 1's buffer, frees its own
+        assert out[1][1] == "alloc,open,free"  # its mapping failed: only frees its own
+        assert "rank 1" in out[0][0]

@@ -1,8 +1,8 @@
 """Head-sharded prefill on 2 GPUs: both transports against one-GPU results.
 
-peer: every rank's kernel stores its heads into every rank's symmetric output
-buffer over NVLink (wfattn_prefill_gather); the gathered output must be
-bit-identical to the same kernel run for all heads on one GPU.  nccl: chunked
+peer: every rank's kernel stores its heads into every rank's output buffer
+(CUDA IPC mappings, wfattn_peer_*) over NVLink (wfattn_prefill_gather); the
+gathered output must be bit-identical to the same kernel run for all heads on one GPU.  nccl: chunked
 all-gathers of per-rank outputs; within the bf16 tolerance of that result.
 Skipped on boxes with fewer than two GPUs.
 """
@@ -54,6 +54,7 @@ def _worker(rank, world, port, path):
         o = out.float()
         res[transport] = (sp.transport, bool(torch.equal(out.contiguous(), ref)),
                           float((o - ref.float()).abs().max() / ref.float().abs().max()))
+        sp.close()
     np.save(f"{path}.{rank}.npy", np.array([res["peer"][1], res["nccl"][2],
                                              res["peer"][0] == "peer"], dtype=np.float64))
     dist.barrier()

@@ -20,7 +20,8 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 EXPORTED_SYMBOLS = (
     "wfattn_version", "wfattn_status_string", "wfattn_last_error", "wfattn_attention",
     "wfattn_prefill", "wfattn_prefill_gather", "wfattn_decode_workspace_size", "wfattn_decode",
-    "wfattn_decode_noalloc", "wfattn_device_status",
+    "wfattn_decode_noalloc", "wfattn_device_status", "wfattn_peer_alloc", "wfattn_peer_open",
+    "wfattn_peer_close", "wfattn_peer_free",
 )
 
 
@@ -34,6 +35,12 @@ class WfattnError(RuntimeError):
 
 class Dim3(ctypes.Structure):
     _fields_ = [("x", ctypes.c_uint), ("y", ctypes.c_uint), ("z", ctypes.c_uint)]
+
+
+class PeerHandle(ctypes.Structure):
+    """wfattn_peer_handle_t: 64 opaque bytes naming a device buffer across processes."""
+
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 _lib = None
@@ -75,6 +82,15 @@ def load() -> ctypes.CDLL:
                                           _i64p, _vp, _vp, _i64p, ctypes.c_float, _vp]
     lib.wfattn_device_status.restype = ctypes.c_int
     lib.wfattn_device_status.argtypes = [_vp, ctypes.c_int]
+    lib.wfattn_peer_alloc.restype = ctypes.c_int
+    lib.wfattn_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(_vp),
+                                      ctypes.POINTER(PeerHandle)]
+    lib.wfattn_peer_open.restype = ctypes.c_int
+    lib.wfattn_peer_open.argtypes = [ctypes.POINTER(PeerHandle), ctypes.c_int, ctypes.POINTER(_vp)]
+    lib.wfattn_peer_close.restype = ctypes.c_int
+    lib.wfattn_peer_close.argtypes = [_vp, ctypes.c_int]
+    lib.wfattn_peer_free.restype = ctypes.c_int
+    lib.wfattn_peer_free.argtypes = [_vp, ctypes.c_int]
     _lib = lib
     return lib
 

@@ -17,5 +17,9 @@ bool make_bf16_map_64x128(CUtensorMap *m, const void *base, int64_t B, int64_t H
 // The same with a box of {64, box_rows, 1, 1} (box_rows <= 256).
 bool make_bf16_map_64xR(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
                         const Strides3 &st, int box_rows);
+// Box {box_cols, box_rows, 1, 1} (box_cols * 2 bytes a multiple of 16) with
+// 128-byte swizzle (box_cols == 64) or none (shared-memory tile row-major).
+bool make_bf16_map(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
+                   const Strides3 &st, int box_cols, int box_rows, bool swizzle128);
 
 }  // namespace wfattn

@@ -10,6 +10,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <mutex>
 #include <string>
@@ -406,6 +407,92 @@ wfattn_status_t wfattn_device_status(void *stream, int clear) {
   if (word & kDevBadLengthMask)
     return fail(WFATTN_INVALID_ARG, "a kv_lens entry was outside [1, max_kv_len] (status 0x%x)",
                 word);
+  return WFATTN_OK;
+}
+
+// Peer buffers: plain cudaMalloc memory exported and imported with CUDA IPC
+// handles.  An imported buffer is an ordinary peer mapping over NVLink; no
+// multicast object is involved.
+static_assert(sizeof(wfattn_peer_handle_t) == sizeof(cudaIpcMemHandle_t),
+              "wfattn_peer_handle_t must hold a cudaIpcMemHandle_t");
+
+namespace {
+
+// Makes `device` current for the lifetime of the guard, then restores the previous device.
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t enter(int device) {
+    cudaError_t err = cudaGetDevice(&prev);
+    if (err != cudaSuccess) {
+      prev = -1;
+      return err;
+    }
+    return cudaSetDevice(device);
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+wfattn_status_t wfattn_peer_alloc(size_t bytes, int device, void **ptr,
+                                  wfattn_peer_handle_t *handle) {
+  t_last_error.clear();
+  if (!ptr || !handle || bytes == 0 || device < 0)
+    return fail(WFATTN_INVALID_ARG, "peer_alloc needs bytes > 0, a device and out pointers");
+  *ptr = nullptr;
+  DeviceScope scope;
+  cudaError_t err = scope.enter(device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+  void *p = nullptr;
+  err = cudaMalloc(&p, bytes);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMalloc(peer buffer)");
+  cudaIpcMemHandle_t h;
+  err = cudaIpcGetMemHandle(&h, p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(err, "cudaIpcGetMemHandle");
+  }
+  memcpy(handle->bytes, &h, sizeof(h));
+  *ptr = p;
+  return WFATTN_OK;
+}
+
+wfattn_status_t wfattn_peer_open(const wfattn_peer_handle_t *handle, int device, void **ptr) {
+  t_last_error.clear();
+  if (!ptr || !handle || device < 0)
+    return fail(WFATTN_INVALID_ARG, "peer_open needs a handle, a device and an out pointer");
+  *ptr = nullptr;
+  DeviceScope scope;
+  cudaError_t err = scope.enter(device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->bytes, sizeof(h));
+  err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaIpcOpenMemHandle");
+  return WFATTN_OK;
+}
+
+wfattn_status_t wfattn_peer_close(void *ptr, int device) {
+  t_last_error.clear();
+  if (!ptr || device < 0) return fail(WFATTN_INVALID_ARG, "peer_close needs a pointer");
+  DeviceScope scope;
+  cudaError_t err = scope.enter(device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+  err = cudaIpcCloseMemHandle(ptr);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaIpcCloseMemHandle");
+  return WFATTN_OK;
+}
+
+wfattn_status_t wfattn_peer_free(void *ptr, int device) {
+  t_last_error.clear();
+  if (!ptr || device < 0) return fail(WFATTN_INVALID_ARG, "peer_free needs a pointer");
+  DeviceScope scope;
+  cudaError_t err = scope.enter(device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+  err = cudaFree(ptr);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaFree(peer buffer)");
   return WFATTN_OK;
 }
 

@@ -15,6 +15,7 @@ enum DeviceStatusBits : unsigned int {
 };
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 // Strided [B, H, S, D] view (element strides, unit head_dim stride).
 struct Strides3 {

@@ -5,11 +5,11 @@ per GPU) split the heads evenly and compute them with no exchange; the only
 exchange is the all-gather of O.  Two transports:
 
 * ``peer`` (bf16 on GPUs, the default there): every rank's full [B, H, S, D]
-  output lives in symmetric memory mapped on all ranks.  The attention kernel
-  stores each finished output tile of its heads into every rank's buffer over
-  NVLink (``wfattn_prefill_gather``), so the gather rides along tile by tile
-  with the compute; one cross-rank barrier ends the step.  Rank r owns heads
-  [r*H/G, (r+1)*H/G).
+  output is a ``peer.PeerBuffer`` mapped on all ranks (CUDA IPC).  The
+  attention kernel stores each finished output tile of its heads into every
+  rank's buffer over NVLink (``wfattn_prefill_gather``), so the gather rides
+  along tile by tile with the compute; one cross-rank barrier ends the step.
+  Rank r owns heads [r*H/G, (r+1)*H/G).
 * ``nccl`` (any dtype or device, and the fallback): the heads are cut into C
   chunks of H/C heads, each chunk split evenly over the ranks: rank r owns
   heads [c*H/C + r*h, c*H/C + (r+1)*h) of chunk c, with h = H/(C*G).  A rank
@@ -86,16 +86,19 @@ class ShardedPrefill:
         self.local_heads = heads // self.world
         self.B, self.H, self.S, self.D = batch, heads, seq, head_dim
         self.transport = "nccl"
+        self.peer = None
         peer_ok = (self.world > 1 and torch.device(device).type == "cuda"
                    and dtype == torch.bfloat16 and head_dim == 64 and compute is None
                    and chunks in (None, 1))
         if transport == "peer" and not peer_ok:
             raise ValueError("the peer transport needs bf16, head_dim 64, CUDA and >1 rank")
         if transport in ("auto", "peer") and peer_ok:
-            try:
+            from .peer import PeerSetupError
+
+            try:  # collective; on failure every rank raises, so all of them fall back
                 self._setup_peer(dtype, device)
                 self.transport = "peer"
-            except Exception:
+            except PeerSetupError:
                 if transport == "peer":
                     raise
         if self.transport == "peer":
@@ -110,17 +113,23 @@ class ShardedPrefill:
         self.compute = compute or _default_compute
 
     def _setup_peer(self, dtype, device) -> None:
-        import torch.distributed._symmetric_memory as symm_mem
+        from .peer import PeerBuffer
 
-        group_name = (self.group or dist.group.WORLD).group_name
-        shape = (self.B, self.H, self.S, self.D)
-        self.full = symm_mem.empty(shape, dtype=dtype, device=device)
-        self.hdl = symm_mem.rendezvous(self.full, group_name)
-        h0 = self.rank * self.local_heads
-        # this rank's heads inside every rank's output buffer (peer mappings)
-        self.peer_outs = [self.hdl.get_remote_tensor(r, shape, dtype)[:, h0:h0 + self.local_heads]
-                          for r in range(self.world)]
+        self.peer = PeerBuffer((self.B, self.H, self.S, self.D), dtype, device, self.group)
+        self.full = self.peer.tensor
+        # this rank's heads inside every rank's output buffer, as mapped on this GPU
+        off = self.rank * self.local_heads * self.full.stride(1) * self.full.element_size()
+        self.peer_outs = [p + off for p in self.peer.ptrs]
+        self.out_strides = self.full.stride()[:3]
         self._sync = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def close(self) -> None:
+        """Collective with the peer transport (every rank calls it): releases the mapped
+        output buffers.  Without it they live until the process exits."""
+        if self.transport == "peer" and self.peer is not None:
+            self.full = None
+            self.peer.close()
+            self.peer = None
 
     def chunk_heads(self, c: int) -> tuple[int, int]:
         """Global head range of this rank's part of chunk c."""
@@ -152,9 +161,10 @@ class ShardedPrefill:
         """This rank's heads only, without the final synchronisation (peer transport: the
         kernel still stores into every rank's buffer)."""
         if self.transport == "peer":
-            from .warpforth import attention_gather
+            from .warpforth import attention_gather_ptrs
 
-            attention_gather(qs[0], ks[0], vs[0], self.peer_outs, causal=causal, scale=scale)
+            attention_gather_ptrs(qs[0], ks[0], vs[0], self.peer_outs, self.out_strides,
+                                  causal=causal, scale=scale)
             return
         for c in range(self.chunks):
             self._compute_chunk(c, qs[c], ks[c], vs[c], causal, scale)

@@ -105,35 +105,54 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool
     return out
 
 
+def _check_bf16_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t)
+        if t.dtype != torch.bfloat16 or t.dim() != 4 or t.stride(3) != 1:
+            raise ValueError(f"{name} must be a bf16 [B, H, S, D] view with a unit last stride")
+    b, h, _, d = q.shape
+    sk = k.shape[2]
+    if k.shape != (b, h, sk, d) or v.shape != (b, h, sk, d):
+        raise ValueError("shape mismatch")
+
+
 def attention_gather(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                      outs: list[torch.Tensor], *, causal: bool = True,
                      scale: float | None = None) -> None:
     """bf16 attention of q/k/v ([B, H, S, 64] CUDA views) written to every tensor in ``outs``.
 
-    Each ``outs[i]`` is a [B, H, Sq, 64] bf16 view with the same strides, possibly of another
-    GPU's memory (a peer mapping of a symmetric buffer): the kernel stores every finished
-    output tile to all of them, so a head-sharded prefill needs no separate all-gather.  The
-    caller synchronises with the other GPUs after the call.
+    Each ``outs[i]`` is a [B, H, Sq, 64] bf16 view with the same strides.  The kernel
+    stores every finished output tile to all of them.
     """
-    for name, t in (("q", q), ("k", k), ("v", v)):
-        _require_cuda(name, t)
-        if t.dtype != torch.bfloat16 or t.dim() != 4 or t.stride(3) != 1:
-            raise ValueError(f"{name} must be a bf16 [B, H, S, D] view with a unit last stride")
-    b, h, sq, d = q.shape
-    sk = k.shape[2]
-    if k.shape != (b, h, sk, d) or v.shape != (b, h, sk, d):
-        raise ValueError("shape mismatch")
+    _check_bf16_qkv(q, k, v)
     if not 1 <= len(outs) <= 8:
         raise ValueError("outs must hold 1 to 8 tensors")
     for o in outs:
         if o.shape != q.shape or o.dtype != q.dtype or o.stride() != outs[0].stride():
             raise ValueError("every output must match q's shape and dtype with one set of strides")
+    attention_gather_ptrs(q, k, v, [o.data_ptr() for o in outs], outs[0].stride()[:3],
+                          causal=causal, scale=scale)
+
+
+def attention_gather_ptrs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                          out_ptrs: list[int], out_strides: tuple[int, int, int], *,
+                          causal: bool = True, scale: float | None = None) -> None:
+    """``attention_gather`` with raw output addresses: each ``out_ptrs[i]`` is the start of
+    a [B, H, Sq, 64] bf16 view with element strides ``out_strides`` = (batch, head, seq),
+    e.g. this rank's heads inside every rank's ``peer.PeerBuffer`` as mapped on this GPU.
+    The stores into other GPUs' buffers are complete when the kernel is; the caller
+    synchronises with those GPUs afterwards."""
+    _check_bf16_qkv(q, k, v)
+    if not 1 <= len(out_ptrs) <= 8:
+        raise ValueError("out_ptrs must hold 1 to 8 addresses")
+    b, h, sq, d = q.shape
     lib = _lib.load()
-    st = [_lib.strides_arg(t.stride()[:3]) for t in (q, k, v, outs[0])]
-    ptrs = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+    st = [_lib.strides_arg(t.stride()[:3]) for t in (q, k, v)]
+    ptrs = (ctypes.c_void_p * len(out_ptrs))(*out_ptrs)
     _lib.check(lib.wfattn_prefill_gather(
-        b, h, sq, sk, d, _ptr(q), st[0], _ptr(k), st[1], _ptr(v), st[2], ptrs, len(outs), st[3],
-        float(scale) if scale else 0.0, 1 if causal else 0, _stream_handle(q.device)))
+        b, h, sq, k.shape[2], d, _ptr(q), st[0], _ptr(k), st[1], _ptr(v), st[2], ptrs,
+        len(out_ptrs), _lib.strides_arg(out_strides), float(scale) if scale else 0.0,
+        1 if causal else 0, _stream_handle(q.device)))
 
 
 class DecodeWorkspace:

@@ -249,6 +249,21 @@ def test_bf16_long_sequence_rows_sampled(wf):
     assert _bf16_rel_err(out[..., :256, :], ref[..., :256, :]) <= BF16_REL_TOL
 
 
+def test_bf16_two_tile_kernel_grouped_item_order(wf):
+    # 18 blocks of 256 rows per head and >= 32 items per SM: the two-tile kernel
+    # walks its items in groups of 8 blocks of one head, the last group partial
+    b, h, s = 2, 136, 4500
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q, k, v = (torch.randn(b, h, s, 64, generator=g, device="cuda").bfloat16() for _ in range(3))
+    out = torch.full_like(q, float("nan"))
+    wf.attention(q, k, v, out=out)
+    assert torch.isfinite(out.float()).all()
+    for bi, hi in ((0, 0), (1, 135), (0, 77), (1, 8)):
+        sl = (slice(bi, bi + 1), slice(hi, hi + 1))
+        ref = _oracle(q[sl].cpu(), k[sl].cpu(), v[sl].cpu())
+        assert _bf16_rel_err(out[sl].float().cpu().numpy(), ref) <= BF16_REL_TOL, (bi, hi)
+
+
 def test_bf16_deterministic_and_output_fully_written(wf):
     q, k, v = (_randn((3, 5, 777, 64), 700 + i, torch.bfloat16).cuda() for i in range(3))
     o1 = torch.full((3, 5, 777, 64), float("nan"), dtype=torch.bfloat16, device="cuda")

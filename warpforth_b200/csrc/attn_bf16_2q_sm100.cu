@@ -85,6 +85,7 @@ struct Params {
   int64_t B, H, Sq, Sk;
   int64_t n_pairs;  // 256-row query blocks per (batch, head)
   int64_t n_items;  // n_pairs * B * H
+  uint32_t group;   // consecutive blocks of one (batch, head) in the item order
   char *o;
   int64_t os_b, os_h, os_s;
   float scale_log2;
@@ -107,16 +108,29 @@ struct Item {
 };
 
 // Items are numbered heaviest first (the causal blocks nearest the end of the
-// sequence see the most keys).  CTA i takes item r*G + i in even rounds r and
-// r*G + (G-1-i) in odd ones (G = grid size): the snake order evens out the
-// CTAs' totals.  Returns false past the last item.
+// sequence see the most keys), in groups of p.group consecutive 256-row
+// blocks of one (batch, head): the group's CTAs run at the same time and
+// share that head's K/V tiles in L2 (group 1: every CTA on another head).
+// CTA i takes item r*G + i in even rounds r and r*G + (G-1-i) in odd ones
+// (G = grid size): the snake order evens out the CTAs' totals.  Returns
+// false past the last item.
 __device__ __forceinline__ bool item_of(const Params &p, int k, Item &it) {
   // 32-bit arithmetic: the launcher keeps n_items below 2^31.
   const uint32_t G = gridDim.x;
   const uint32_t idx = (uint32_t)k * G + ((k & 1) ? G - 1 - blockIdx.x : blockIdx.x);
   if ((int64_t)idx >= p.n_items) return false;
   const uint32_t BH = (uint32_t)(p.B * p.H), H = (uint32_t)p.H;
-  const uint32_t blk = idx / BH, bh = idx - blk * BH;
+  const uint32_t NP = (uint32_t)p.n_pairs, gs = p.group, n_full = NP / gs;
+  uint32_t blk, bh;
+  if (idx < n_full * gs * BH) {
+    const uint32_t g = idx / (gs * BH), r = idx - g * (gs * BH);
+    bh = r / gs;
+    blk = g * gs + (r - bh * gs);
+  } else {  // the last, partial group
+    const uint32_t gl = NP - n_full * gs, r = idx - n_full * gs * BH;
+    bh = r / gl;
+    blk = n_full * gs + (r - bh * gl);
+  }
   const int64_t qp = p.n_pairs - 1 - blk;
   it.b = (int)(bh / H);
   it.h = (int)(bh - (uint32_t)it.b * H);
@@ -653,6 +667,10 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   if (p.n_items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   // Persistent: one CTA per SM walks the items (fewer CTAs for small problems).
   const int64_t blocks = p.n_items < dev.sm_count ? p.n_items : dev.sm_count;
+  // Groups of 8 blocks per head cut HBM reads when every CTA has many items
+  // (long sequences, 16+ blocks per head); with few items per CTA the plain
+  // heaviest-first order balances the CTAs better.
+  p.group = (p.n_pairs >= 16 && p.n_items >= 32 * blocks) ? 8 : 1;
   prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, outs, p);
   return cudaGetLastError();
 }

@@ -103,3 +103,39 @@ def test_check_raises_with_library_message():
     lib = _lib.load()
     with pytest.raises(_lib.WfattnError, match="INVALID_ARG"):
         _lib.check(_prefill(lib, b=0))
+
+
+def _integration_blocks(lang: str) -> list[str]:
+    return re.findall(rf"```{lang}\n(.*?)```", (ROOT / "INTEGRATION.md").read_text(), re.S)
+
+
+def test_integration_c_example_compiles(tmp_path):
+    """The multi-GPU C example (peer buffers + wfattn_prefill_gather) compiles as written."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    (block,) = _integration_blocks("c")
+    src = tmp_path / "example.c"
+    src.write_text(
+        "#include <stdint.h>\n#include \"wfattn.h\"\n"
+        "void step(int64_t B, int64_t H, int64_t S, int G, int rank, int dev,\n"
+        "          const void *q_local, const int64_t *q_strides, const void *k_local,\n"
+        "          const int64_t *k_strides, const void *v_local, const int64_t *v_strides,\n"
+        "          void *stream) {\n" + block + "}\n")
+    res = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-Wno-unused-result", "-c",
+                          "-I", str(ROOT / "include"), str(src), "-o", str(tmp_path / "e.o")],
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+
+
+def test_integration_python_binding_reports_errors():
+    """The ctypes binding shown for demo/warpforth.py loads the library and surfaces its
+    error text (a host-side argument error; no GPU call is made)."""
+    block = _integration_blocks("python")[0]
+    ns: dict = {}
+    exec(block.replace('"warpforth_b200/lib/libwfattn.so"', repr(str(_lib.LIB_PATH))), ns)
+    lib = ns["lib"]
+    assert lib.wfattn_attention(None, None, None, None, 4, 4, None, None, None) == _lib.INVALID_ARG
+    assert "null" in lib.wfattn_last_error().decode()

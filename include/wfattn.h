@@ -115,10 +115,13 @@ WFATTN_API wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t head
  * the output goes to every one of outputs[0 .. n_outputs-1] (1 <= n_outputs
  * <= 8), each a [B, H, Sq, 64] bf16 view with the strides o_strides, e.g. this
  * rank's heads inside every rank's full output buffer when the buffers are
- * mapped across GPUs (wfattn_peer_alloc / wfattn_peer_open).  The kernel
- * stores each finished output tile to all of them as it goes, so the transfer
- * overlaps the computation.  The stores are complete when the kernel is; a caller that
- * writes into other GPUs' buffers synchronises with those GPUs afterwards.
+ * mapped across GPUs (wfattn_peer_alloc / wfattn_peer_open).  outputs[0] must
+ * be memory of the calling GPU (WFATTN_INVALID_ARG otherwise): it receives
+ * TMA stores; outputs[1..] receive plain 16-byte stores from the kernel (no
+ * TMA touches another GPU's memory).  Every finished output tile goes to all
+ * of them as the kernel runs, so the transfer overlaps the computation.  The
+ * stores are complete when the kernel is; a caller that writes into other
+ * GPUs' buffers synchronises with those GPUs afterwards.
  */
 WFATTN_API wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_q,
                                                  int64_t seq_k, int64_t head_dim, const void *q,

@@ -264,6 +264,22 @@ def test_bf16_two_tile_kernel_grouped_item_order(wf):
         assert _bf16_rel_err(out[sl].float().cpu().numpy(), ref) <= BF16_REL_TOL, (bi, hi)
 
 
+def test_bf16_gather_writes_every_destination_identically(wf):
+    # wfattn_prefill_gather: outputs[0] takes the kernel's TMA stores, outputs[1..] its
+    # plain 16-byte stores (the path that writes other GPUs' buffers); here all three are
+    # on this GPU, with one strided [B, S, H, D] layout and ragged rows (S = 300)
+    b, h, s = 2, 80, 300
+    q, k, v = (_randn((b, h, s, 64), 900 + i, torch.bfloat16).cuda() for i in range(3))
+    outs = [torch.full((b, s, h, 64), float("nan"), dtype=torch.bfloat16,
+                       device="cuda").transpose(1, 2) for _ in range(3)]
+    wf.attention_gather(q, k, v, outs)
+    ref = wf.attention(q, k, v)
+    for o in outs:
+        assert torch.equal(o, ref)
+    with pytest.raises(ValueError):
+        wf.attention_gather(q, k, v, [])
+
+
 def test_bf16_deterministic_and_output_fully_written(wf):
     q, k, v = (_randn((3, 5, 777, 64), 700 + i, torch.bfloat16).cuda() for i in range(3))
     o1 = torch.full((3, 5, 777, 64), float("nan"), dtype=torch.bfloat16, device="cuda")

@@ -86,18 +86,14 @@ struct Params {
   int64_t n_pairs;  // 256-row query blocks per (batch, head)
   int64_t n_items;  // n_pairs * B * H
   uint32_t group;   // consecutive blocks of one (batch, head) in the item order
-  char *o;
+  // Further destinations of the output (e.g. other GPUs' buffers mapped into
+  // this one), written with plain 16-byte stores; strides os_* are shared.
+  char *remote[kMaxOutputPeers - 1];
+  int n_remote;
   int64_t os_b, os_h, os_s;
   float scale_log2;
   int causal;
   unsigned int *status;
-};
-
-// Output tensor maps: the output buffer, or one per GPU that receives a copy
-// (the all-gather of a head-sharded prefill done by the kernel's own stores).
-struct OutMaps {
-  CUtensorMap m[kMaxOutputPeers];
-  int n;
 };
 
 // One work item: 256 query rows (tiles A and B) of one (batch, head).
@@ -201,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_bf16_2q_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v,
-                           const __grid_constant__ OutMaps outs, const Params p) {
+                           const __grid_constant__ CUtensorMap tm_o, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~uintptr_t(1023));
@@ -243,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == kTmaVWarp && lane == 0) {
     ptx::prefetch_tmap(&tm_v);
-    for (int r = 0; r < outs.n; ++r) ptx::prefetch_tmap(&outs.m[r]);
+    ptx::prefetch_tmap(&tm_o);
   }
   if (warp == kMmaQkWarp) {
     if (lane == 0) trace(1, 1);
@@ -591,12 +587,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        // one store per destination (other GPUs' buffers over NVLink), all
-        // reading the same slab; they complete as one bulk group
-        for (int r = 0; r < outs.n; ++r)
-          ptx::tma_store_4d(&outs.m[r], ptx::smem_u32(stage), 0, (int)(q_tile + 32 * (warp & 3)),
-                            it.h, it.b);
+        ptx::tma_store_4d(&tm_o, ptx::smem_u32(stage), 0, (int)(q_tile + 32 * (warp & 3)), it.h,
+                          it.b);
         ptx::bulk_commit_group();
+      }
+      if (p.n_remote > 0) {
+        // The further destinations (the all-gather of a head-sharded prefill:
+        // other GPUs' buffers, written over NVLink): 16-byte stores read back
+        // from the slab, eight lanes per 128-byte row so every row goes out as
+        // whole lines; rows past Sq are skipped.
+        const int64_t row0 = q_tile + 32 * (warp & 3);
+        const int64_t head = it.b * p.os_b + it.h * p.os_h;
+        const int ch = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + (lane >> 3);
+          const uint4 w =
+              *reinterpret_cast<const uint4 *>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
+          if (row0 + r < p.Sq) {
+            const int64_t off = 2 * (head + (row0 + r) * p.os_s) + 16 * ch;
+#pragma unroll
+            for (int d = 0; d < kMaxOutputPeers - 1; ++d)
+              if (d < p.n_remote) *reinterpret_cast<uint4 *>(p.remote[d] + off) = w;
+          }
+        }
       }
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 15 : 9, k);
     }
@@ -638,13 +652,12 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
       !make_bf16_map_64x128(&tk, a.k, a.B, a.H, a.Sk, a.ks) ||
       !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
     return cudaErrorInvalidValue;
-  OutMaps outs;
-  outs.n = a.n_peers > 0 ? a.n_peers : 1;
-  if (outs.n > kMaxOutputPeers) return cudaErrorInvalidValue;
-  for (int r = 0; r < outs.n; ++r)
-    if (!make_bf16_map_64xR(&outs.m[r], a.n_peers > 0 ? a.o_peers[r] : a.o, a.B, a.H, a.Sq, a.os,
-                            32))
-      return cudaErrorInvalidValue;
+  // The first destination (on this GPU) takes TMA stores of 32-row slabs; the
+  // others, plain stores.
+  CUtensorMap to;
+  if (a.n_peers > kMaxOutputPeers ||
+      !make_bf16_map_64xR(&to, a.n_peers > 0 ? a.o_peers[0] : a.o, a.B, a.H, a.Sq, a.os, 32))
+    return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
     return cudaErrorInvalidValue;
   cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(prefill_bf16_2q_kernel),
@@ -656,7 +669,9 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   p.Sq = a.Sq;
   p.Sk = a.Sk;
   p.n_pairs = (a.Sq + 2 * kBM - 1) / (2 * kBM);
-  p.o = static_cast<char *>(a.o);
+  p.n_remote = a.n_peers > 1 ? a.n_peers - 1 : 0;
+  for (int d = 0; d < kMaxOutputPeers - 1; ++d)
+    p.remote[d] = d < p.n_remote ? static_cast<char *>(a.o_peers[d + 1]) : nullptr;
   p.os_b = a.os.b;
   p.os_h = a.os.h;
   p.os_s = a.os.s;
@@ -671,7 +686,7 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   // (long sequences, 16+ blocks per head); with few items per CTA the plain
   // heaviest-first order balances the CTAs better.
   p.group = (p.n_pairs >= 16 && p.n_items >= 32 * blocks) ? 8 : 1;
-  prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, outs, p);
+  prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }
 

@@ -261,7 +261,18 @@ wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_
   a.n_peers = n_outputs;
   st = check_bf16(a);
   if (st != WFATTN_OK) return st;
-  const cudaError_t err = launch_prefill_bf16_2q(a, dev, static_cast<cudaStream_t>(stream));
+  // outputs[0] takes the kernel's TMA stores: it must be this GPU's own memory
+  // (the kernel writes other GPUs' buffers with plain stores only).
+  cudaPointerAttributes attr;
+  cudaError_t err = cudaPointerGetAttributes(&attr, outputs[0]);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(err, "cudaPointerGetAttributes(outputs[0])");
+  }
+  if (attr.type != cudaMemoryTypeDevice || attr.device != dev.device)
+    return fail(WFATTN_INVALID_ARG, "outputs[0] must be device memory of the calling GPU (%d)",
+                dev.device);
+  err = launch_prefill_bf16_2q(a, dev, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
   return WFATTN_OK;
 }

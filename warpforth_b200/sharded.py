@@ -117,9 +117,12 @@ class ShardedPrefill:
 
         self.peer = PeerBuffer((self.B, self.H, self.S, self.D), dtype, device, self.group)
         self.full = self.peer.tensor
-        # this rank's heads inside every rank's output buffer, as mapped on this GPU
+        # this rank's heads inside every rank's output buffer, as mapped on this GPU;
+        # its own buffer first (the kernel's TMA stores go to the first destination
+        # only, the other GPUs' buffers get plain stores)
         off = self.rank * self.local_heads * self.full.stride(1) * self.full.element_size()
-        self.peer_outs = [p + off for p in self.peer.ptrs]
+        order = [self.rank] + [r for r in range(self.world) if r != self.rank]
+        self.peer_outs = [self.peer.ptrs[r] + off for r in order]
         self.out_strides = self.full.stride()[:3]
         self._sync = torch.zeros(1, dtype=torch.int32, device=device)
 

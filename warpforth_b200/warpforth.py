@@ -140,8 +140,9 @@ def attention_gather_ptrs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     """``attention_gather`` with raw output addresses: each ``out_ptrs[i]`` is the start of
     a [B, H, Sq, 64] bf16 view with element strides ``out_strides`` = (batch, head, seq),
     e.g. this rank's heads inside every rank's ``peer.PeerBuffer`` as mapped on this GPU.
-    The stores into other GPUs' buffers are complete when the kernel is; the caller
-    synchronises with those GPUs afterwards."""
+    ``out_ptrs[0]`` must be this GPU's own memory (it takes TMA stores; the others get
+    plain stores).  The stores into other GPUs' buffers are complete when the kernel is;
+    the caller synchronises with those GPUs afterwards."""
     _check_bf16_qkv(q, k, v)
     if not 1 <= len(out_ptrs) <= 8:
         raise ValueError("out_ptrs must hold 1 to 8 addresses")

@@ -12,7 +12,8 @@ commits completing in issue order per issuing thread, and checks:
 * every parity wait, each time it is polled, finds its barrier at the awaited
   phase or one past it;
 * no buffer is overwritten while it is still read (K/V ring stages, Q slots,
-  S, P and O of each tile) and none is read before it is written;
+  S, P and O of each tile, the output staging slab that a TMA store reads
+  asynchronously) and none is read before it is written;
 * every role finishes (no deadlock).
 
 Each softmax tile is one actor here (its 128 threads arrive together); the
@@ -66,7 +67,7 @@ class ProtocolError(AssertionError):
     pass
 
 
-WAITS = ("q_empty", "k_empty", "v_empty", "s_free", "o_free", "o_done_before_p")
+WAITS = ("q_empty", "k_empty", "v_empty", "s_free", "o_free", "o_done_before_p", "slab_read")
 
 
 def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -> None:
@@ -177,6 +178,12 @@ def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -
             yield ("wait", f"o_done{t}", ns - 1)
             yield ("check", ("pv_done", t, ns))
             yield ("do", ("o_read", t))
+            # the output staging slab: the previous item's TMA store must have
+            # read it (bulk wait_group.read) before it is written again
+            if "slab_read" not in omit:
+                yield ("slab_wait", t)
+            yield ("check", ("slab_free", t))
+            yield ("store", t)
             yield ("arrive", f"o_free{t}")
 
     roles = {"kp": k_producer(), "vp": v_producer(), "qk": qk_issuer(), "pv": pv_issuer(),
@@ -184,6 +191,7 @@ def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -
     cur = {r: next(g, None) for r, g in roles.items()}
     pipes: dict[str, list] = {"qk": [], "pv": []}
     loads: list = []
+    stores: list = []  # tiles whose slab an output TMA store is still reading
 
     def check(what) -> None:
         kind = what[0]
@@ -216,6 +224,9 @@ def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -
             _, t, n = what
             if any(("pv", t, i) not in done["pv"] for i in range(max(0, n - 2), n)):
                 raise ProtocolError(f"tile {t}: P/O touched at step {n} with a P.V pending")
+        elif kind == "slab_free":
+            if what[1] in stores:
+                raise ProtocolError(f"tile {what[1]}'s staging slab rewritten while a store reads it")
         elif kind == "o_read":
             _, t, items_done = what
             if state["o_read_items"][t] < items_done:
@@ -225,6 +236,10 @@ def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -
         runnable = []
         for r, op in cur.items():
             if op is None:
+                continue
+            if op[0] == "slab_wait":
+                if op[1] not in stores:
+                    runnable.append(r)
                 continue
             if op[0] == "wait":
                 have, want = c(op[1]), op[2]
@@ -238,11 +253,17 @@ def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -
         runnable += [f"pipe_{p}" for p, q in pipes.items() if q]
         if loads:
             runnable.append("tma")
+        # odd seeds: a store finishes reading its slab only when nothing else can move
+        if stores and (not (seed & 1) or not runnable):
+            runnable.append("store_read")
         if not runnable:
             if all(op is None for op in cur.values()):
                 return
             raise ProtocolError(f"deadlock: {cur}")
         r = rnd.choice(runnable)
+        if r == "store_read":
+            stores.pop(rnd.randrange(len(stores)))
+            continue
         if r == "tma":
             bar, tag = loads.pop(rnd.randrange(len(loads)))
             count[bar] = c(bar) + 1
@@ -264,6 +285,8 @@ def simulate(items: list[list[int]], seed: int, omit: frozenset = frozenset()) -
             pipes[op[1]].append(("commit", op[2]))
         elif op[0] == "arrive":  # the arrival of the last of the role's threads
             count[op[1]] = c(op[1]) + 1
+        elif op[0] == "store":
+            stores.append(op[1])
         elif op[0] == "check":
             check(op[1])
         elif op[0] == "do":

@@ -205,7 +205,12 @@ def _peer_worker(rank, world, port, result_path, case):
         if status:
             raise _lib.WfattnError(status, "fake failure")
 
-    peer._lib = types.SimpleNamespace(load=lambda: fake, check=check, PeerHandle=_lib.PeerHandle,
+    def load():
+        if case == "load" and rank == 0:
+            raise _lib.WfattnError(_lib.CUDA_ERROR, "library missing")
+        return fake
+
+    peer._lib = types.SimpleNamespace(load=load, check=check, PeerHandle=_lib.PeerHandle,
                                       WfattnError=_lib.WfattnError)
     try:
         peer.PeerBuffer((2, 4, 8, 64), torch.bfloat16, torch.device("cuda", rank))
@@ -217,10 +222,11 @@ def _peer_worker(rank, world, port, result_path, case):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["alloc", "open"])
+@pytest.mark.parametrize("case", ["alloc", "open", "load"])
 def test_peer_buffer_setup_failure_is_raised_on_every_rank(tmp_path, case):
-    """One rank's failed allocation (rank 0) or mapping (rank 1) makes every rank raise
-    PeerSetupError after releasing what it set up, so all ranks can fall back together."""
+    """One rank's failed library load or allocation (rank 0) or mapping (rank 1) makes every
+    rank raise PeerSetupError after releasing what it set up, so all ranks can fall back
+    together."""
     port = _free_port()
     path = str(tmp_path / "res")
     mp.start_processes(_peer_worker, args=(2, port, path, case), nprocs=2, join=True,
@@ -228,7 +234,11 @@ def test_peer_buffer_setup_failure_is_raised_on_every_rank(tmp_path, case):
     out = {r: open(f"{path}.{r}.status").read().split("\n") for r in range(2)}
     for r in range(2):
         assert out[r][0].startswith("PeerSetupError: rank "), out[r]
-    if case == "alloc":
+    if case == "load":
+        assert out[0][1] == ""  # never reached the library
+        assert out[1][1] == "alloc,free"
+        assert "rank 0: " in out[1][0] and "library missing" in out[1][0]
+    elif case == "alloc":
         assert out[0][1] == "alloc"  # nothing to release
         assert out[1][1] == "alloc,free"  # never maps, frees its own buffer
         assert "rank 0" in out[1][0]

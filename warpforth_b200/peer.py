@@ -58,14 +58,15 @@ class PeerBuffer:
         self.shape = tuple(int(s) for s in shape)
         itemsize = torch.empty((), dtype=dtype).element_size()
         nbytes = math.prod(self.shape) * itemsize
-        lib = _lib.load()
         self._own: int | None = None
         self._opened: list[int] = []
         self.ptrs: list[int] = []
         handle = _lib.PeerHandle()
         err = ""
         ptr = ctypes.c_void_p()
-        try:
+        lib = None
+        try:  # a failure here still takes part in the collectives below
+            lib = _lib.load()
             _lib.check(lib.wfattn_peer_alloc(nbytes, self.index, ctypes.byref(ptr),
                                              ctypes.byref(handle)))
             self._own = ptr.value
@@ -94,7 +95,8 @@ class PeerBuffer:
             dist.all_gather_object(errors, err, group=group)
         bad = [(r, e) for r, e in enumerate(errors) if e]
         if bad:
-            self._release(lib)
+            if lib is not None:
+                self._release(lib)
             raise PeerSetupError("; ".join(f"rank {r}: {e}" for r, e in bad))
         self.tensor = torch.as_tensor(_DeviceArray(self._own, self.shape, itemsize),
                                       device=self.device).view(dtype)

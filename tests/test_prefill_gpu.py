@@ -278,6 +278,14 @@ def test_bf16_gather_writes_every_destination_identically(wf):
         assert torch.equal(o, ref)
     with pytest.raises(ValueError):
         wf.attention_gather(q, k, v, [])
+    # the first destination takes TMA stores and must be this GPU's memory: pinned host
+    # memory there is rejected on the host before any launch
+    from warpforth_b200 import _lib
+
+    host = torch.empty((b, s, h, 64), dtype=torch.bfloat16, pin_memory=True).transpose(1, 2)
+    with pytest.raises(_lib.WfattnError, match="outputs\\[0\\]"):
+        wf.attention_gather_ptrs(q, k, v, [host.data_ptr(), outs[0].data_ptr()],
+                                 outs[0].stride()[:3])
 
 
 def test_bf16_deterministic_and_output_fully_written(wf):

@@ -266,12 +266,13 @@ def test_bf16_two_tile_kernel_grouped_item_order(wf):
 
 def test_bf16_gather_writes_every_destination_identically(wf):
     # wfattn_prefill_gather: outputs[0] takes the kernel's TMA stores, outputs[1..] its
-    # plain 16-byte stores (the path that writes other GPUs' buffers); here all three are
-    # on this GPU, with one strided [B, S, H, D] layout and ragged rows (S = 300)
+    # plain 16-byte stores (the path that writes other GPUs' buffers); here all eight (the
+    # most, as on 8 GPUs) are on this GPU, with one strided [B, S, H, D] layout and ragged
+    # rows (S = 300)
     b, h, s = 2, 80, 300
     q, k, v = (_randn((b, h, s, 64), 900 + i, torch.bfloat16).cuda() for i in range(3))
     outs = [torch.full((b, s, h, 64), float("nan"), dtype=torch.bfloat16,
-                       device="cuda").transpose(1, 2) for _ in range(3)]
+                       device="cuda").transpose(1, 2) for _ in range(8)]
     wf.attention_gather(q, k, v, outs)
     ref = wf.attention(q, k, v)
     for o in outs:

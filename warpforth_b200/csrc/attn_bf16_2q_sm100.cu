@@ -1,9 +1,12 @@
 // attn_bf16_2q_sm100.cu -- causal flash attention (prefill), bf16 in/out, f32
 // accumulation on tcgen05 tensor cores; two 128-row query tiles per CTA.
 //
-// One CTA (one per SM) computes 256 query rows of one (batch, head) as two
-// 128-row tiles A and B that share every K/V tile loaded by TMA (half the
-// L2 -> shared-memory traffic per FLOP of one tile per CTA).
+// Persistent: one CTA per SM walks work items of 256 query rows of one
+// (batch, head), heaviest first (item_of), each as two 128-row tiles A and B
+// that share every K/V tile loaded by TMA (half the L2 -> shared-memory
+// traffic per FLOP of one tile per CTA).  All ring and barrier phases are
+// counted across items, so the next item's loads and first S overlap the
+// current item's tail.
 //
 //   warp 1 (TMA, K)   Q_A, Q_B of each work item (two slots); K_j tiles into a 3-deep ring
 //   warp 2 (TMA, V)   V_j tiles into their own 3-deep ring.  K and V have
@@ -18,7 +21,12 @@
 //                     (TMEM lane = row, 32x32b loads; warp w reads lanes
 //                     32*(w%4)..+31, the sub-partition it may access): the
 //                     row max and row sum need no shuffles and each thread
-//                     packs its own P row.
+//                     packs its own P row.  At the end of an item each warp
+//                     writes its 32 output rows to a swizzled staging slab
+//                     and one TMA store into the local output; for a fused
+//                     all-gather the same warp copies the slab to every
+//                     further destination (other GPUs' buffers) with plain
+//                     16-byte stores.
 //
 // TMEM (512 columns): S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384)
 //                     O_A [384,448) O_B [448,512).

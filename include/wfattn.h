@@ -115,11 +115,12 @@ WFATTN_API wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t head
  * the output goes to every one of outputs[0 .. n_outputs-1] (1 <= n_outputs
  * <= 8), each a [B, H, Sq, 64] bf16 view with the strides o_strides, e.g. this
  * rank's heads inside every rank's full output buffer when the buffers are
- * mapped across GPUs (wfattn_peer_alloc / wfattn_peer_open).  outputs[0] must
- * be memory of the calling GPU (WFATTN_INVALID_ARG otherwise): it receives
- * TMA stores; outputs[1..] receive plain 16-byte stores from the kernel (no
- * TMA touches another GPU's memory).  Every finished output tile goes to all
- * of them as the kernel runs, so the transfer overlaps the computation.  The
+ * mapped across GPUs (wfattn_peer_alloc / wfattn_peer_open).  q, k, v and
+ * outputs[0] must be device memory of the calling GPU (WFATTN_INVALID_ARG
+ * otherwise): they are read and written by TMA; outputs[1..] receive plain
+ * 16-byte stores from the kernel (no TMA touches another GPU's memory).
+ * Every finished output tile goes to all of them as the kernel runs, so the
+ * transfer overlaps the computation.  The
  * stores are complete when the kernel is; a caller that writes into other
  * GPUs' buffers synchronises with those GPUs afterwards.
  */
@@ -147,6 +148,8 @@ WFATTN_API wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, i
  *           kv_lens[b] are never read)
  * o:        f32 [B, H, D] with o_strides = {batch, head} (NULL = contiguous)
  * head_dim must be 64.  scale <= 0 selects 1/sqrt(head_dim).
+ * batch * heads and max_kv_len must each be at most 2^31 - 1
+ * (WFATTN_INVALID_ARG otherwise; wfattn_decode_workspace_size returns 0).
  * workspace: device scratch of at least wfattn_decode_workspace_size() bytes,
  *           16-byte aligned, owned by the caller; calls that share a
  *           workspace must be ordered on one stream.

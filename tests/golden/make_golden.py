@@ -85,8 +85,9 @@ class CapturingRunner:
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-    ref = _load_reference_tests(ref_root)
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <root of the reference tree>")
+    ref = _load_reference_tests(Path(sys.argv[1]))
 
     kats = {}
     for test_name, rel in (("test_naive_attention_f64", 1e-6),

@@ -139,3 +139,23 @@ def test_integration_python_binding_reports_errors():
     lib = ns["lib"]
     assert lib.wfattn_attention(None, None, None, None, 4, 4, None, None, None) == _lib.INVALID_ARG
     assert "null" in lib.wfattn_last_error().decode()
+
+
+def test_decode_shape_bounds_are_checked_without_overflow():
+    """batch*heads and max_kv_len are bounded on the host, so a huge shape can neither wrap
+    the workspace size to a small number nor reach a launch (no GPU call is made)."""
+    lib = _lib.load()
+    assert lib.wfattn_decode_workspace_size(64, 25, 4096, 64) == 64 * 25 * 16 * 66 * 4
+    huge = 1 << 62
+    assert lib.wfattn_decode_workspace_size(huge, huge, 4096, 64) == 0
+    assert lib.wfattn_decode_workspace_size(1 << 31, 1, 4096, 64) == 0
+    assert lib.wfattn_decode_workspace_size(1, 1, 1 << 31, 64) == 0
+    for b, h, lmax in ((huge, huge, 4096), (1 << 31, 1, 256), (1, 1, 1 << 40)):
+        st = lib.wfattn_decode(b, h, 64, lmax, 16, None, 16, None, 16, None, 16, 16, None, 0.0,
+                               16, 1 << 40, None)
+        assert st == _lib.INVALID_ARG
+        assert b"2^31-1" in lib.wfattn_last_error()
+        st = lib.wfattn_decode_noalloc(b, h, 64, lmax, 16, None, 16, None, 16, None, 16, 16,
+                                       None, 0.0, None)
+        assert st == _lib.INVALID_ARG
+        assert b"2^31-1" in lib.wfattn_last_error()

@@ -106,9 +106,9 @@ def test_decode_config4_shape(wf):
     vc = torch.randn(64, 25, 4096, 64, dtype=torch.bfloat16)
     q = torch.randn(64, 25, 64, dtype=torch.bfloat16)
     out = wf.decode(q.cuda(), kc.cuda(), vc.cuda(), lens.cuda()).cpu().numpy()
-    sel = [0, 7, 63]
-    ref = _ref(q[sel], kc[sel], vc[sel], lens[sel])
-    assert _rel(out[sel], ref) <= BF16_REL_TOL
+    # all 64 sequences x 25 heads against the f64 oracle (under 1 GFLOP)
+    assert np.isfinite(out).all()
+    assert _rel(out, _ref(q, kc, vc, lens)) <= BF16_REL_TOL
     wf.device_status(clear=True)
 
 

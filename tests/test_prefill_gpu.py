@@ -121,16 +121,12 @@ def test_f32_hf_strided_views_and_noncausal_and_cross_lengths(wf):
     assert np.abs(dst.transpose(1, 2).cpu().numpy() - ref).max() <= F32_ABS_TOL
 
 
-def test_f32_gpt2_batched_config3_subset(wf):
-    # [8, 12, 1024, 64] f32, seed 2: every head on the GPU, a head subset on the oracle
+def test_f32_gpt2_batched_config3_all_heads(wf):
+    # [8, 12, 1024, 64] f32, seed 2: every row of every head against the f64 oracle
     torch.manual_seed(2)
     q, k, v = (torch.randn(8, 12, 1024, 64) for _ in range(3))
     out = wf.attention(q.cuda(), k.cuda(), v.cuda()).cpu().numpy()
-    ref = _oracle(q, k, v, bh_range=(0, 96), row_range=(896, 1024))
-    assert np.abs(out[..., 896:, :] - ref[..., 896:, :]).max() <= F32_ABS_TOL
-    ref = _oracle(q, k, v, bh_range=(90, 96))
-    assert np.abs(out.reshape(96, 1024, 64)[90:] - ref.reshape(96, 1024, 64)[90:]).max() <= \
-        F32_ABS_TOL
+    assert np.abs(out - _oracle(q, k, v)).max() <= F32_ABS_TOL
 
 
 # ---------------------------------------------------------------- bf16 (tcgen05)
@@ -227,10 +223,9 @@ def test_bf16_config3_against_oracle_and_f32_kernel(wf):
     q, k, v = (torch.randn(8, 12, 1024, 64) for _ in range(3))
     qb, kb, vb = (t.bfloat16() for t in (q, k, v))
     out = wf.attention(qb.cuda(), kb.cuda(), vb.cuda()).float().cpu().numpy()
-    # the full oracle is ~13 GFLOP of f64; check the first 8 heads exactly
-    sub = _oracle(qb, kb, vb, bh_range=(0, 8))
-    assert _bf16_rel_err(out.reshape(1, 96, 1024, 64)[:, :8],
-                         sub.reshape(1, 96, 1024, 64)[:, :8]) <= BF16_REL_TOL
+    # every one of the 96 heads against the f64 oracle (~13 GFLOP, seconds on the host cores)
+    ref = _oracle(qb, kb, vb)
+    assert _bf16_rel_err(out, ref) <= BF16_REL_TOL
     # size-independent property: the bf16 kernel tracks the f32 kernel on every head
     of32 = wf.attention(qb.float().cuda(), kb.float().cuda(), vb.float().cuda()).cpu().numpy()
     assert _bf16_rel_err(out, of32) <= BF16_REL_TOL

@@ -460,13 +460,25 @@ cudaError_t decode_noalloc_scratch(void **ptr) {
   return cudaSuccess;
 }
 
+bool decode_shape_ok(int64_t B, int64_t H, int64_t max_len) {
+  // kv_lens are int32, so a longer cache is never read past 2^31 - 1 rows; the
+  // combine kernel's grid covers B*H in blocks of 4 (grid.x < 2^31).
+  int64_t bh = 0;
+  return B >= 1 && H >= 1 && max_len >= 1 && max_len <= INT32_MAX &&
+         !__builtin_mul_overflow(B, H, &bh) && bh <= INT32_MAX;
+}
+
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t) {
+  // Within decode_shape_ok's bounds: B*H < 2^31 and nch < 2^23, so the
+  // partial count stays below 2^54 and the byte count below 2^63.
+  if (!decode_shape_ok(B, H, max_len)) return 0;
   const int64_t nch = (max_len + kChunk - 1) / kChunk;
   return (size_t)(B * H * nch) * kPartFloats * sizeof(float);
 }
 
 cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
   if (a.ks.s != kD || a.vs.s != kD) return cudaErrorInvalidValue;  // rows must be contiguous
+  if (!decode_shape_ok(a.B, a.H, a.max_len)) return cudaErrorInvalidValue;
   DecParams p;
   p.B = a.B;
   p.H = a.H;

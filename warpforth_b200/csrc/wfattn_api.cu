@@ -261,18 +261,23 @@ wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_
   a.n_peers = n_outputs;
   st = check_bf16(a);
   if (st != WFATTN_OK) return st;
-  // outputs[0] takes the kernel's TMA stores: it must be this GPU's own memory
-  // (the kernel writes other GPUs' buffers with plain stores only).
-  cudaPointerAttributes attr;
-  cudaError_t err = cudaPointerGetAttributes(&attr, outputs[0]);
-  if (err != cudaSuccess) {
-    cudaGetLastError();
-    return cuda_fail(err, "cudaPointerGetAttributes(outputs[0])");
+  // q, k, v (TMA loads) and outputs[0] (TMA stores) must be this GPU's own
+  // memory: the kernel reaches other GPUs' buffers only through the plain
+  // stores to outputs[1..].
+  const void *local[4] = {q, k, v, outputs[0]};
+  const char *names[4] = {"q", "k", "v", "outputs[0]"};
+  for (int i = 0; i < 4; ++i) {
+    cudaPointerAttributes attr;
+    const cudaError_t perr = cudaPointerGetAttributes(&attr, local[i]);
+    if (perr != cudaSuccess) {
+      cudaGetLastError();
+      return cuda_fail(perr, "cudaPointerGetAttributes");
+    }
+    if (attr.type != cudaMemoryTypeDevice || attr.device != dev.device)
+      return fail(WFATTN_INVALID_ARG, "%s must be device memory of the calling GPU (%d)",
+                  names[i], dev.device);
   }
-  if (attr.type != cudaMemoryTypeDevice || attr.device != dev.device)
-    return fail(WFATTN_INVALID_ARG, "outputs[0] must be device memory of the calling GPU (%d)",
-                dev.device);
-  err = launch_prefill_bf16_2q(a, dev, static_cast<cudaStream_t>(stream));
+  cudaError_t err = launch_prefill_bf16_2q(a, dev, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
   return WFATTN_OK;
 }
@@ -299,8 +304,8 @@ wfattn_status_t wfattn_attention(const float *Q, const float *K, const float *V,
 
 size_t wfattn_decode_workspace_size(int64_t batch, int64_t heads, int64_t max_kv_len,
                                     int64_t head_dim) {
-  if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1) return 0;
-  return decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
+  if (head_dim < 1) return 0;
+  return decode_workspace_bytes(batch, heads, max_kv_len, head_dim);  // 0 for a bad shape
 }
 
 wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, int64_t max_kv_len,
@@ -314,6 +319,10 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
     return fail(WFATTN_INVALID_ARG, "null tensor pointer");
   if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1)
     return fail(WFATTN_INVALID_ARG, "sizes must be >= 1");
+  if (!decode_shape_ok(batch, heads, max_kv_len))
+    return fail(WFATTN_INVALID_ARG,
+                "decode needs batch*heads <= 2^31-1 and max_kv_len <= 2^31-1 (B=%lld H=%lld "
+                "max_kv_len=%lld)", (long long)batch, (long long)heads, (long long)max_kv_len);
   if (head_dim != 64) return fail(WFATTN_UNSUPPORTED, "decode supports head_dim == 64 only");
   const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
   if (!workspace || workspace_bytes < need)
@@ -373,6 +382,10 @@ wfattn_status_t wfattn_decode_noalloc(int64_t batch, int64_t heads, int64_t head
   t_last_error.clear();
   if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1)
     return fail(WFATTN_INVALID_ARG, "sizes must be >= 1");
+  if (!decode_shape_ok(batch, heads, max_kv_len))
+    return fail(WFATTN_INVALID_ARG,
+                "decode needs batch*heads <= 2^31-1 and max_kv_len <= 2^31-1 (B=%lld H=%lld "
+                "max_kv_len=%lld)", (long long)batch, (long long)heads, (long long)max_kv_len);
   const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
   if (need > kDecodeNoAllocScratchBytes)
     return fail(WFATTN_INVALID_ARG,

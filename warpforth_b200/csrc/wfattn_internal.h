@@ -72,6 +72,10 @@ cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,
 cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
                                    cudaStream_t stream);
 
+// Decode shapes the kernels index safely: sizes >= 1, max_len <= 2^31 - 1,
+// B*H <= 2^31 - 1 (checked without overflow).
+bool decode_shape_ok(int64_t B, int64_t H, int64_t max_len);
+// Workspace bytes of a decode call (0 when decode_shape_ok fails).
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t D);
 cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream);
 

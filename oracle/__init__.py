@@ -36,8 +36,10 @@ _i32p = ctypes.POINTER(ctypes.c_int32)
 
 
 def build() -> Path:
-    """Compile wf_oracle.c with the committed Makefile."""
-    subprocess.run(["make", "-C", str(_HERE)], check=True, capture_output=True, text=True)
+    """Compile wf_oracle.c with the committed Makefile, and copy the reference's compiled
+    attention kernel into ``_ref/`` where the reference tree is present (``make ref``)."""
+    subprocess.run(["make", "-C", str(_HERE), "all", "ref"], check=True, capture_output=True,
+                   text=True)
     return _LIB_PATH
 
 

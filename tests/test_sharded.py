@@ -246,3 +246,103 @@ def test_peer_buffer_setup_failure_is_raised_on_every_rank(tmp_path, case):
         assert out[0][1] == "alloc,open,close,free"  # unmaps rank 1's buffer, frees its own
         assert out[1][1] == "alloc,open,free"  # its mapping failed: only frees its own
         assert "rank 1" in out[0][0]
+
+
+class _ShmPeerBuffer:
+    """Stands in for peer.PeerBuffer on CPU ranks: every rank's buffer is a file in the
+    test's folder that all ranks map (shared memory), so a rank's writes land in another
+    rank's buffer as the kernel's peer stores do over NVLink.  ``ptrs[r]`` is the address
+    of rank r's mapping in this process."""
+
+    def __init__(self, shape, dtype, device, group, root):
+        import math
+
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        n = math.prod(shape)
+        self.maps = [None] * self.world
+        self.maps[self.rank] = torch.from_file(f"{root}/peer{self.rank}.bin", shared=True,
+                                               size=n, dtype=dtype)
+        dist.barrier(group)  # every rank's file exists
+        for r in range(self.world):
+            if r != self.rank:
+                self.maps[r] = torch.from_file(f"{root}/peer{r}.bin", shared=True, size=n,
+                                               dtype=dtype)
+        self.tensor = self.maps[self.rank].view(shape)
+        self.ptrs = [m.data_ptr() for m in self.maps]
+
+    def close(self):
+        dist.barrier()
+
+
+def _race_worker(rank, world, port, result_path, single_slot):
+    """Four steps with different inputs; rank 1 keeps reading each step's output for a while
+    (a slow consumer) while rank 0 runs ahead into the next step."""
+    import time
+
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
+    from warpforth_b200 import sharded
+
+    root = os.path.dirname(result_path)
+    maps = []
+
+    def fake_buffer(shape, dtype, device, group):
+        buf = _ShmPeerBuffer(shape, dtype, device, group, root)
+        maps.extend(buf.maps)
+        return buf
+
+    def fake_gather(q, k, v, out_ptrs, out_strides, *, causal, scale):
+        # the "kernel": this rank's output (here q itself) stored into every destination
+        for ptr in out_ptrs:
+            (m,) = [m for m in maps
+                    if m.data_ptr() <= ptr < m.data_ptr() + m.numel() * m.element_size()]
+            off = (ptr - m.data_ptr()) // m.element_size()
+            torch.as_strided(m, q.shape, (*out_strides, 1), off).copy_(q)
+
+    sharded._peer_capable = lambda device, dtype, head_dim: True
+    sharded._peer_buffer = fake_buffer
+    sharded._launch_gather = fake_gather
+    b, h, s, d = 2, 4, 16, 64
+    sp = sharded.ShardedPrefill(b, h, s, d, dtype=torch.bfloat16, device=torch.device("cpu"),
+                                transport="peer")
+    assert sp.transport == "peer"
+    if single_slot:  # the layout without double buffering: every call writes one slot
+        sp.peer_outs = (sp.peer_outs[0], sp.peer_outs[0])
+        sp.slots = (sp.slots[0], sp.slots[0])
+    report = []
+    for step in range(4):
+        g = torch.Generator().manual_seed(100 + step)
+        q = torch.randn(b, h, s, d, generator=g).bfloat16()
+        out = sp(sp.shard(q), sp.shard(q), sp.shard(q))
+        seen = out.clone()
+        if rank == 1:
+            time.sleep(0.5)  # still using this step's output
+        report.append(f"{step}:{int(torch.equal(seen, q))}{int(torch.equal(out, seen))}")
+    sp.close()
+    with open(f"{result_path}.{rank}.status", "w") as f:
+        f.write(" ".join(report))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("single_slot", [False, True])
+def test_peer_output_survives_a_rank_running_ahead(tmp_path, single_slot):
+    """The peer transport's output of call n must stay intact on a slow rank while a fast
+    rank runs call n+1 (its stores go to the other slot) until the slow rank's next call.
+    The single-slot layout is run too, to show the test sees the overwrite it guards
+    against."""
+    port = _free_port()
+    path = str(tmp_path / "res")
+    mp.start_processes(_race_worker, args=(2, port, path, single_slot), nprocs=2, join=True,
+                       start_method="spawn")
+    slow = open(f"{path}.1.status").read().split()
+    fast = open(f"{path}.0.status").read().split()
+    # step:<result right when first read><still intact after the slow read>
+    assert [r[2] for r in slow] == ["1"] * 4
+    assert [r[2] for r in fast] == ["1"] * 4
+    if single_slot:
+        assert "0" in [r[3] for r in slow[:3]], slow  # rank 0's next call overwrote it
+    else:
+        assert [r[3] for r in slow] == ["1"] * 4, slow

@@ -2,9 +2,12 @@
 
 peer: every rank's kernel stores its heads into every rank's output buffer
 (CUDA IPC mappings, wfattn_peer_*) over NVLink (wfattn_prefill_gather); the
-gathered output must be bit-identical to the same kernel run for all heads on one GPU.  nccl: chunked
-all-gathers of per-rank outputs; within the bf16 tolerance of that result.
-Skipped on boxes with fewer than two GPUs.
+gathered output must be bit-identical to the same kernel run for all heads on
+one GPU.  nccl: chunked all-gathers of per-rank outputs; within the bf16
+tolerance of that result.  Three steps with different inputs, and rank 1 reads
+each step's output only after a ~25 ms device delay, while rank 0 runs ahead:
+its next step must not overwrite what rank 1 has yet to read.  Skipped on boxes
+with fewer than two GPUs.
 """
 
 from __future__ import annotations
@@ -41,19 +44,30 @@ def _worker(rank, world, port, path):
     from warpforth_b200.sharded import ShardedPrefill
 
     b, h, s, d = 2, 16, 640, 64
-    g = torch.Generator().manual_seed(7)
-    q, k, v = (torch.randn(b, h, s, d, generator=g).bfloat16().to(dev) for _ in range(3))
-    ref = torch.empty_like(q)
-    wf.attention_gather(q, k, v, [ref])  # the two-tile kernel for every head, one GPU
+    steps = []
+    for step in range(3):  # different inputs every step
+        g = torch.Generator().manual_seed(7 + step)
+        q, k, v = (torch.randn(b, h, s, d, generator=g).bfloat16().to(dev) for _ in range(3))
+        ref = torch.empty_like(q)
+        wf.attention_gather(q, k, v, [ref])  # the two-tile kernel for every head, one GPU
+        steps.append((q, k, v, ref))
+    torch.cuda.synchronize()
     res = {}
     for transport in ("peer", "nccl"):
         sp = ShardedPrefill(b, h, s, d, dtype=torch.bfloat16, device=dev, transport=transport)
-        for _ in range(2):  # the second step reuses the buffers
+        exact, rel = True, 0.0
+        for q, k, v, ref in steps:
             out = sp(sp.shard(q), sp.shard(k), sp.shard(v))
+            if rank == 1:
+                # a slow consumer: its copy of this step's output runs ~25 ms later on the
+                # GPU, while rank 0 is already in the next step
+                torch.cuda._sleep(50_000_000)
+            seen = out.clone()
+            exact &= bool(torch.equal(seen, ref))
+            o = seen.float()
+            rel = max(rel, float((o - ref.float()).abs().max() / ref.float().abs().max()))
         torch.cuda.synchronize()
-        o = out.float()
-        res[transport] = (sp.transport, bool(torch.equal(out.contiguous(), ref)),
-                          float((o - ref.float()).abs().max() / ref.float().abs().max()))
+        res[transport] = (sp.transport, exact, rel)
         sp.close()
     np.save(f"{path}.{rank}.npy", np.array([res["peer"][1], res["nccl"][2],
                                              res["peer"][0] == "peer"], dtype=np.float64))

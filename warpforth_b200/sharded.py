@@ -4,12 +4,16 @@ Every (batch, head) pair of attention is independent, so G ranks (one process
 per GPU) split the heads evenly and compute them with no exchange; the only
 exchange is the all-gather of O.  Two transports:
 
-* ``peer`` (bf16 on GPUs, the default there): every rank's full [B, H, S, D]
-  output is a ``peer.PeerBuffer`` mapped on all ranks (CUDA IPC).  The
-  attention kernel stores each finished output tile of its heads into every
-  rank's buffer over NVLink (``wfattn_prefill_gather``), so the gather rides
-  along tile by tile with the compute; one cross-rank barrier ends the step.
-  Rank r owns heads [r*H/G, (r+1)*H/G).
+* ``peer`` (bf16 on GPUs, the default there): every rank holds two full
+  [B, H, S, D] output slots in one ``peer.PeerBuffer`` mapped on all ranks
+  (CUDA IPC).  The attention kernel stores each finished output tile of its
+  heads into every rank's buffer over NVLink (``wfattn_prefill_gather``), so
+  the gather rides along tile by tile with the compute; one cross-rank barrier
+  ends the step.  Rank r owns heads [r*H/G, (r+1)*H/G).  Calls alternate
+  between the two slots: a rank that starts call n+1 early writes the other
+  slot, and it cannot start call n+2 (which reuses call n's slot) before every
+  rank has reached the barrier of call n+1, i.e. before every rank has queued
+  or finished whatever it does with call n's output.
 * ``nccl`` (any dtype or device, and the fallback): the heads are cut into C
   chunks of H/C heads, each chunk split evenly over the ranks: rank r owns
   heads [c*H/C + r*h, c*H/C + (r+1)*h) of chunk c, with h = H/(C*G).  A rank
@@ -56,6 +60,23 @@ def default_chunks(heads: int, world: int) -> int:
 ComputeFn = Callable[..., torch.Tensor]
 
 
+def _peer_capable(device, dtype, head_dim) -> bool:
+    """Whether the kernel-side peer gather can run for this device, dtype and head size."""
+    return torch.device(device).type == "cuda" and dtype == torch.bfloat16 and head_dim == 64
+
+
+def _peer_buffer(shape, dtype, device, group):
+    from .peer import PeerBuffer
+
+    return PeerBuffer(shape, dtype, device, group)
+
+
+def _launch_gather(q, k, v, out_ptrs, out_strides, *, causal, scale):
+    from .warpforth import attention_gather_ptrs
+
+    attention_gather_ptrs(q, k, v, out_ptrs, out_strides, causal=causal, scale=scale)
+
+
 def _default_compute(q, k, v, *, causal, scale, out):
     from .warpforth import attention
 
@@ -65,12 +86,19 @@ def _default_compute(q, k, v, *, causal, scale, out):
 class ShardedPrefill:
     """Runs this rank's share of a [B, H, S, D] attention and all-gathers O.
 
-    The output buffer (``full`` for the peer transport, ``gathered`` =
-    [C, G, h, B, S, D] for NCCL) is allocated once and reused.  ``__call__``
-    takes this rank's q/k/v as per-chunk lists of [B, h, S, D] views (from
-    ``shard`` of the full tensors or ``split_local`` of a rank-local tensor;
-    one chunk with the peer transport) and returns the full [B, H, S, D]
-    output.  ``transport`` is "auto" (peer where possible), "peer" or "nccl".
+    The output buffers (two slots of [B, H, S, D] for the peer transport,
+    ``gathered`` = [C, G, h, B, S, D] for NCCL) are allocated once and reused.
+    ``__call__`` takes this rank's q/k/v as per-chunk lists of [B, h, S, D]
+    views (from ``shard`` of the full tensors or ``split_local`` of a
+    rank-local tensor; one chunk with the peer transport) and returns the full
+    [B, H, S, D] output.  ``transport`` is "auto" (peer where possible), "peer"
+    or "nccl".
+
+    Lifetime of the returned tensor: it holds this call's output until the
+    call after next (peer transport: the two slots alternate; NCCL: the
+    gather buffer is reused by the next call).  Whatever reads it must be
+    queued on the current stream, or finished on the host, before this rank's
+    next call; other ranks cannot overwrite it before then.
     """
 
     def __init__(self, batch: int, heads: int, seq: int, head_dim: int, *,
@@ -87,9 +115,8 @@ class ShardedPrefill:
         self.B, self.H, self.S, self.D = batch, heads, seq, head_dim
         self.transport = "nccl"
         self.peer = None
-        peer_ok = (self.world > 1 and torch.device(device).type == "cuda"
-                   and dtype == torch.bfloat16 and head_dim == 64 and compute is None
-                   and chunks in (None, 1))
+        peer_ok = (self.world > 1 and _peer_capable(device, dtype, head_dim)
+                   and compute is None and chunks in (None, 1))
         if transport == "peer" and not peer_ok:
             raise ValueError("the peer transport needs bf16, head_dim 64, CUDA and >1 rank")
         if transport in ("auto", "peer") and peer_ok:
@@ -113,24 +140,28 @@ class ShardedPrefill:
         self.compute = compute or _default_compute
 
     def _setup_peer(self, dtype, device) -> None:
-        from .peer import PeerBuffer
-
-        self.peer = PeerBuffer((self.B, self.H, self.S, self.D), dtype, device, self.group)
-        self.full = self.peer.tensor
-        # this rank's heads inside every rank's output buffer, as mapped on this GPU;
-        # its own buffer first (the kernel's TMA stores go to the first destination
-        # only, the other GPUs' buffers get plain stores)
-        off = self.rank * self.local_heads * self.full.stride(1) * self.full.element_size()
+        # two output slots [2, B, H, S, D] in one buffer per rank, mapped on every rank
+        self.peer = _peer_buffer((2, self.B, self.H, self.S, self.D), dtype, device, self.group)
+        buf = self.peer.tensor
+        self.slots = (buf[0], buf[1])
+        esz = buf.element_size()
+        # this rank's heads inside every rank's output slot, as mapped on this GPU; its
+        # own buffer first (the kernel's TMA stores go to the first destination only,
+        # the other GPUs' buffers get plain stores)
+        head_off = self.rank * self.local_heads * buf.stride(2) * esz
+        slot_bytes = buf.stride(0) * esz
         order = [self.rank] + [r for r in range(self.world) if r != self.rank]
-        self.peer_outs = [self.peer.ptrs[r] + off for r in order]
-        self.out_strides = self.full.stride()[:3]
+        self.peer_outs = tuple([self.peer.ptrs[r] + s * slot_bytes + head_off for r in order]
+                               for s in (0, 1))
+        self.out_strides = buf.stride()[1:4]
+        self.calls = 0  # peer calls so far; call n writes slot n % 2
         self._sync = torch.zeros(1, dtype=torch.int32, device=device)
 
     def close(self) -> None:
         """Collective with the peer transport (every rank calls it): releases the mapped
         output buffers.  Without it they live until the process exits."""
         if self.transport == "peer" and self.peer is not None:
-            self.full = None
+            self.slots = None
             self.peer.close()
             self.peer = None
 
@@ -149,8 +180,9 @@ class ShardedPrefill:
         return [t[:, c * self.ch:(c + 1) * self.ch] for c in range(self.chunks)]
 
     def output_view(self) -> torch.Tensor:
+        """The full [B, H, S, D] output of the last call."""
         if self.transport == "peer":
-            return self.full
+            return self.slots[(self.calls - 1) & 1]
         return self.gathered.view(self.H, self.B, self.S, self.D).permute(1, 0, 2, 3)
 
     def _compute_chunk(self, c, q, k, v, causal, scale):
@@ -162,12 +194,11 @@ class ShardedPrefill:
                       vs: Sequence[torch.Tensor], *, causal: bool = True,
                       scale: float | None = None) -> None:
         """This rank's heads only, without the final synchronisation (peer transport: the
-        kernel still stores into every rank's buffer)."""
+        kernel still stores into every rank's buffer, into the slot the next call
+        writes)."""
         if self.transport == "peer":
-            from .warpforth import attention_gather_ptrs
-
-            attention_gather_ptrs(qs[0], ks[0], vs[0], self.peer_outs, self.out_strides,
-                                  causal=causal, scale=scale)
+            _launch_gather(qs[0], ks[0], vs[0], self.peer_outs[self.calls & 1],
+                           self.out_strides, causal=causal, scale=scale)
             return
         for c in range(self.chunks):
             self._compute_chunk(c, qs[c], ks[c], vs[c], causal, scale)
@@ -177,12 +208,15 @@ class ShardedPrefill:
                  scale: float | None = None) -> torch.Tensor:
         if self.transport == "peer":
             self.compute_local(qs, ks, vs, causal=causal, scale=scale)
+            self.calls += 1
             # A one-element NCCL all-reduce as the cross-rank barrier: once it is
             # done on this rank, every rank's attention kernel (queued before its
             # all-reduce) has completed its stores into this rank's buffer.  It is
-            # bounded by the process group's timeout.
+            # bounded by the process group's timeout.  It also keeps every rank
+            # from starting the call after next -- the next writer of this
+            # call's slot -- before this rank has queued the next call.
             dist.all_reduce(self._sync, group=self.group)
-            return self.full
+            return self.output_view()
         works = []
         for c in range(self.chunks):
             self._compute_chunk(c, qs[c], ks[c], vs[c], causal, scale)

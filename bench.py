@@ -2,7 +2,7 @@
 """Benchmark of the WarpForth attention hot path on B200 (libwfattn).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wfattn|reference]
-                    [--workload long_prefill|prefill|prefill_f32|decode]
+                    [--workload long_prefill|prefill|prefill_f32|decode|gpt2|gpt2_cached|head_call]
 
 For N > 1 launch one process per GPU:
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
@@ -10,19 +10,30 @@ For N > 1 launch one process per GPU:
 
 Workloads (all synthetic, seeded):
   long_prefill (default)  causal prefill [16, 48, 8192, 64] bf16, q/k/v = randn (seed 4);
-                          heads split evenly over the N ranks, O all-gathered (NCCL).
+                          heads split evenly over the N ranks, O all-gathered.
                           One step = the whole batch.  Total work is fixed (strong scaling).
-  prefill                 causal prefill [8, 12, 1024, 64] bf16, seed 2 (per rank).
+  prefill                 causal prefill [8, 12, 1024, 64] bf16, seed 2 (GPT-2 head shape).
   prefill_f32             the same in f32 (the reference-accurate CUDA-core kernel).
   decode                  one-token decode, B=64, H=25, D=64, bf16 cache padded to 4096,
                           kv_lens ~ U[512, 4096] (seed 3); metric = valid KV bytes / s.
+  gpt2                    GPT-2 small random init (seed 1), 32-token prompt, 128 greedy
+                          tokens, use_cache=False (the demo's mode), f32.
+  gpt2_cached             the same generation with the KV cache (use_cache=True).
+  head_call               one GPT-2-small attention call [1, 12, 64, 64] f32, seed 0: latency.
 
 Prints ONE JSON line on rank 0.  `value` is device-timed (CUDA events, inputs
 resident in HBM, max over ranks); `e2e` repeats the step through the public
 API with the inputs copied from pinned host memory and the result read back
-inside the timed region.  `--impl reference` times the CPU restatement of the
-reference kernel (the oracle, f64, all host threads) on a bounded sample of
-the same workload; under torchrun only rank 0 runs it.
+inside the timed region.  The default run (long_prefill) on one GPU also
+measures every other workload and reports each under `workloads`, with its own
+roofline, clocks, e2e, CPU baseline and, where the reference kernel can run
+the case, the reference's compiled kernel timed on the same GPU.
+
+`cpu_baseline` is the demo's torch attention on the host cores
+(scaled_dot_product_attention in f32; stock eager GPT-2 for the generation
+workloads).  `--impl reference` times the CPU restatement of the reference
+kernel (the oracle, f64, all host threads) on a bounded sample of the same
+workload; under torchrun only rank 0 runs it.
 """
 
 from __future__ import annotations
@@ -35,19 +46,20 @@ import statistics
 import subprocess
 import sys
 import time
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_BYTES = 126 * 1024 * 1024
 
 
 @dataclass(frozen=True)
 class Workload:
     name: str
-    kind: str  # "prefill" or "decode"
+    kind: str  # "prefill", "decode", "gpt2" or "head_call"
     B: int
     H: int
     S: int
@@ -56,6 +68,7 @@ class Workload:
     dtype: str  # "bf16" or "f32"
     sharded: bool
     description: str
+    use_cache: bool = False
 
 
 WORKLOADS = {
@@ -72,7 +85,17 @@ WORKLOADS = {
     "gpt2": Workload("gpt2", "gpt2", 1, 12, 128, 64, 1, "f32", False,
                      "GPT-2 small random-init (seed 1), 32-token prompt (seed 1), greedy 128 "
                      "new tokens, use_cache=False, every attention through libwfattn (f32)"),
+    "gpt2_cached": Workload("gpt2_cached", "gpt2", 1, 12, 128, 64, 1, "f32", False,
+                            "GPT-2 small random-init (seed 1), 32-token prompt (seed 1), greedy "
+                            "128 new tokens with the KV cache (use_cache=True): prompt through "
+                            "the prefill kernel, every new token through the decode kernel",
+                            use_cache=True),
+    "head_call": Workload("head_call", "head_call", 1, 12, 64, 64, 0, "f32", False,
+                          "one GPT-2-small attention call [1,12,64,64] f32, seed 0, causal, "
+                          "scale 1/8"),
 }
+# measured beside the default workload on one GPU, reported under "workloads"
+SIDE_WORKLOADS = ("prefill", "prefill_f32", "decode", "gpt2", "gpt2_cached", "head_call")
 
 
 def prefill_flops(w: Workload, heads: int | None = None) -> int:
@@ -95,6 +118,11 @@ def load_peaks() -> tuple[dict, str]:
         except ValueError:
             pass
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+def f32_fma_peak(peaks: dict) -> float:
+    """CUDA-core f32 FMA peak (TFLOP/s): 148 SMs x 128 lanes x 2 FLOP x max SM clock."""
+    return 148 * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
 
 
 # ------------------------------------------------------------------ clocks
@@ -157,8 +185,17 @@ def physical_gpu_indices(n: int) -> list[int]:
     return list(range(n))
 
 
-# ------------------------------------------------------------------ CPU side
-def cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
+def host_threads() -> int:
+    """Host cores this process may run on.  torchrun sets OMP_NUM_THREADS=1 for every rank, so
+    the CPU legs pass their thread count explicitly instead of taking OpenMP's default."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ CPU: the oracle (reference arm)
+def oracle_sample(w: Workload, target_s: float, threads: int) -> dict:
     """Times the oracle (f64 restatement of the reference kernel) on a bounded sample.
 
     Prefill: the last R query rows of `nh` heads of the workload's shape (the
@@ -171,12 +208,22 @@ def cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
     import oracle
 
     if w.kind == "gpt2":
-        return gpt2_cpu_sample(target_s, threads)
+        return gpt2_cpu_sample(w, target_s, threads)
     g = torch.Generator().manual_seed(w.seed)
 
     def bf(t):
         return t.to(torch.bfloat16).float().numpy() if w.dtype == "bf16" else t.numpy()
 
+    if w.kind == "head_call":
+        q, k, v = (torch.randn(w.B, w.H, w.S, w.D, generator=g).numpy() for _ in range(3))
+        n, dt = 0, 0.0
+        t0 = time.perf_counter()
+        while dt < 0.5 * target_s:
+            oracle.attention(q, k, v, nthreads=threads)
+            n += 1
+            dt = time.perf_counter() - t0
+        return {"value": dt / n * 1e6, "unit": "us per call", "seconds": dt,
+                "sample": f"oracle (f64) on the whole [1,12,64,64] call, {n} calls"}
     if w.kind == "prefill":
         def run(nh, rows):
             q, k, v = (bf(torch.randn(1, nh, w.S, w.D, generator=g)) for _ in range(3))
@@ -199,8 +246,7 @@ def cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
                           f"of shape S={w.S}, D={w.D}: {fl:.3e} FLOP in {dt:.2f} s"}
     # decode: whole sequences of the workload (all heads), repeated to reach the target time
     lens = decode_lens().numpy()
-    nb = 4
-    reps = 1
+    nb, reps = 4, 1
     while True:
         sel = lens[:nb]
         q = bf(torch.randn(nb, w.H, 1, w.D, generator=g))
@@ -224,18 +270,113 @@ def cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
                       f"{by} valid KV bytes (bf16-equivalent) in {dt:.2f} s"}
 
 
+# ------------------------------------------------------------------ CPU: the demo's torch attention
+def torch_cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
+    """The demo's torch attention on the host cores: scaled_dot_product_attention in f32 (the
+    golden path of the GPT-2 head call), grown until it takes about `target_s`; stock eager
+    GPT-2 for the generation workloads."""
+    import torch
+    import torch.nn.functional as F
+
+    if w.kind == "gpt2":
+        return gpt2_cpu_sample(w, target_s, threads)
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(w.seed)
+    if w.kind == "head_call":
+        q, k, v = (torch.randn(w.B, w.H, w.S, w.D, generator=g) for _ in range(3))
+        for _ in range(3):
+            F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=w.D ** -0.5)
+        n, dt = 0, 0.0
+        t0 = time.perf_counter()
+        while dt < 0.5 * target_s:
+            F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=w.D ** -0.5)
+            n += 1
+            dt = time.perf_counter() - t0
+        return {"value": dt / n * 1e6, "unit": "us per call", "seconds": dt,
+                "sample": f"torch SDPA f32 on the whole call, {n} calls, {threads} threads"}
+    if w.kind == "prefill":
+        nh = 1
+        while True:
+            q, k, v = (torch.randn(1, nh, w.S, w.D, generator=g) for _ in range(3))
+            F.scaled_dot_product_attention(q[:, :1], k[:, :1], v[:, :1], is_causal=True)
+            t0 = time.perf_counter()
+            F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=w.D ** -0.5)
+            dt = time.perf_counter() - t0
+            if dt >= 0.5 * target_s or nh >= w.B * w.H:
+                break
+            nh = min(w.B * w.H, max(nh + 1, int(nh * min(8.0, target_s / max(dt, 1e-3)))))
+        fl = 4 * w.D * nh * (w.S * (w.S + 1) // 2)
+        return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "seconds": dt,
+                "sample": f"torch SDPA f32 (causal) on {nh} head(s) of S={w.S}, D={w.D}: "
+                          f"{fl:.3e} FLOP in {dt:.2f} s, {threads} threads"}
+    # decode: torch SDPA per sequence over its valid keys (ragged), f32
+    lens = decode_lens()
+    q = torch.randn(w.B, w.H, 1, w.D, generator=g)
+    nb, reps = 8, 1
+    kv = [(torch.randn(1, w.H, int(lens[b]), w.D, generator=g),
+           torch.randn(1, w.H, int(lens[b]), w.D, generator=g)) for b in range(w.B)]
+    while True:
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            for b in range(nb):
+                F.scaled_dot_product_attention(q[b:b + 1], kv[b][0], kv[b][1])
+        dt = time.perf_counter() - t0
+        by = reps * int(lens[:nb].sum()) * w.H * w.D * 2 * 2
+        if dt >= 0.5 * target_s:
+            break
+        grow = min(16.0, max(1.5, target_s / max(dt, 1e-3)))
+        if nb < w.B:
+            nb = min(w.B, int(math.ceil(nb * grow)))
+        else:
+            reps = int(math.ceil(reps * grow))
+    return {"value": by / dt / 1e9, "unit": "GB/s", "seconds": dt,
+            "sample": f"torch SDPA f32 per sequence on {nb} sequence(s) x {w.H} heads, {reps} "
+                      f"pass(es): {by} valid KV bytes (bf16-equivalent) in {dt:.2f} s, "
+                      f"{threads} threads"}
+
+
+def gpt2_cpu_sample(w: Workload, target_s: float, threads: int) -> dict:
+    """Stock eager GPT-2 on the host cores (the demo's torch attention), greedy tokens/s."""
+    import torch
+
+    from warpforth_b200 import gpt2
+
+    torch.set_num_threads(threads)
+    model = gpt2.random_gpt2(seed=1, device="cpu")
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    n = 4
+    while True:
+        t0 = time.perf_counter()
+        gpt2.generate(model, prompt, n, use_cache=w.use_cache)
+        dt = time.perf_counter() - t0
+        if dt >= 0.5 * target_s or n >= 128:
+            break
+        n = min(128, max(n + 1, int(n * min(8.0, target_s / max(dt, 1e-3)))))
+    return {"value": n / dt, "unit": "tokens/s", "seconds": dt,
+            "sample": f"stock eager GPT-2 (torch CPU, {threads} threads, use_cache="
+                      f"{w.use_cache}): the first {n} greedy tokens of the same prompt in "
+                      f"{dt:.2f} s"}
+
+
+def cpu_baseline_of(w: Workload, target_s: float) -> dict:
+    threads = host_threads()
+    r = torch_cpu_sample(w, target_s, threads)
+    return {"value": r["value"], "unit": r["unit"], "cores": threads, "kind": "reference",
+            "what": "the demo's torch attention on the host cores (torch "
+                    "scaled_dot_product_attention f32; stock eager GPT-2 for generation)",
+            "sample": r["sample"]}
+
+
 def run_reference(args, w: Workload) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import oracle
-
     threads = host_threads()
     metric, unit, hib = metric_of(w)
     vals = []
     sample = None
     for i in range(args.warmup + args.steps):
-        r = cpu_sample(w, args.ref_step_seconds, threads)
+        r = oracle_sample(w, args.ref_step_seconds, threads)
         sample = r["sample"]
         if i >= args.warmup:
             vals.append(r["value"])
@@ -258,6 +399,8 @@ def metric_of(w: Workload) -> tuple[str, str, bool]:
         return "decode attention KV GB/s per B200", "GB/s", True
     if w.kind == "gpt2":
         return "GPT-2 gen tokens/s", "tokens/s", True
+    if w.kind == "head_call":
+        return "GPT-2 attention call latency", "us per call", False
     return "causal SDPA TFLOP/s", "TFLOP/s", True
 
 
@@ -266,16 +409,20 @@ def config_of(w: Workload, n: int) -> dict:
            "seed": w.seed}
     if w.kind == "gpt2":
         cfg.update({"model": "gpt2-small (12 layers, d_model 768, vocab 50257, ctx 1024)",
-                    "prompt_len": 32, "new_tokens": w.S, "use_cache": False,
+                    "prompt_len": 32, "new_tokens": w.S, "use_cache": w.use_cache,
                     "parallelism": f"replicas/{n}" if n > 1 else "single",
                     "l2": "not applicable (end-to-end generation)"})
+        return cfg
+    if w.kind == "head_call":
+        cfg.update({"seq_len": w.S, "causal": True, "parallelism": "single",
+                    "l2": "inputs resident in L2 (0.6 MB; a latency measurement)"})
         return cfg
     if w.kind == "prefill":
         cfg.update({"seq_len": w.S, "causal": True,
                     "parallelism": f"heads/{n}" if w.sharded and n > 1 else
                     (f"replicas/{n}" if n > 1 else "single"),
                     "l2": "inputs larger than L2 (126 MB)" if w.S >= 4096 else
-                    "L2 flushed between timed steps (256 MB write)"})
+                    "L2 flushed between timed steps (a 256 MB read)"})
     else:
         cfg.update({"max_kv_len": w.S, "kv_lens": "U[512,4096] seed 3 (sum 142652)",
                     "parallelism": f"replicas/{n}" if n > 1 else "single",
@@ -284,6 +431,594 @@ def config_of(w: Workload, n: int) -> dict:
 
 
 # ------------------------------------------------------------------ GPU side
+class Ctx:
+    """Process-group plumbing shared by the GPU legs."""
+
+    def __init__(self) -> None:
+        import torch
+        import torch.distributed as dist
+
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local_rank)
+        self.dev = torch.device("cuda", self.local_rank)
+        if self.world > 1:
+            from datetime import timedelta
+
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=self.dev)
+        self.stream = torch.cuda.current_stream(self.dev)
+        self.peaks, self.peak_src = load_peaks()
+        self._flush = None
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def min_over_ranks(self, x: float) -> float:
+        return -self.max_over_ranks(-x)
+
+    def flush_l2(self) -> None:
+        """Evicts L2 by reading a 256 MB buffer (twice L2): clean lines, no write-back for
+        the next kernel to pay."""
+        if self._flush is None:
+            self._flush = self.torch.ones(2 * L2_BYTES // 4, dtype=self.torch.float32,
+                                          device=self.dev)
+        self._flush.sum()
+
+    def clocks(self):
+        return ClockSampler(physical_gpu_indices(self.world)) if self.rank == 0 else None
+
+    def event(self):
+        return self.torch.cuda.Event(enable_timing=True)
+
+    def close(self) -> None:
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def time_steps(ctx: Ctx, fn, steps: int, flush: bool) -> tuple[float, list[float], dict | None]:
+    """Times `steps` calls of fn with CUDA events on the current stream; returns the total ms
+    (the sum of per-step times when L2 is flushed between steps), the per-step times and the
+    clocks seen.  Bracketed by a barrier and a synchronize on both sides."""
+    torch = ctx.torch
+    torch.cuda.synchronize()
+    ctx.barrier()
+    clocks = ctx.clocks()
+    if clocks:
+        clocks.start()
+    ev = [(ctx.event(), ctx.event()) for _ in range(steps)]
+    t0, t1 = ctx.event(), ctx.event()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    t0.record(ctx.stream)
+    for i in range(steps):
+        if flush:
+            ctx.flush_l2()
+        ev[i][0].record(ctx.stream)
+        fn()
+        ev[i][1].record(ctx.stream)
+    t1.record(ctx.stream)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    info = clocks.stop() if clocks else None
+    per = [a.elapsed_time(b) for a, b in ev]
+    total = sum(per) if flush else t0.elapsed_time(t1)
+    return total, per, info
+
+
+def graph_of(ctx: Ctx, fn):
+    """fn captured once in a CUDA graph: the device timing then holds the GPU work of the
+    library call, not the Python/ctypes launch path (`e2e` goes through that path)."""
+    torch = ctx.torch
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def timed_e2e(ctx: Ctx, one, steps: int, warmup: int, flush: bool) -> float:
+    """Mean ms of `one` (copies in, compute, copy out) over `steps`, max over ranks."""
+    torch = ctx.torch
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    a, b = ctx.event(), ctx.event()
+    tot = 0.0
+    for _ in range(steps):
+        if flush:
+            ctx.flush_l2()
+        torch.cuda.synchronize()
+        a.record(ctx.stream)
+        one()
+        b.record(ctx.stream)
+        torch.cuda.synchronize()
+        tot += a.elapsed_time(b)
+    ctx.barrier()
+    return ctx.max_over_ranks(tot / steps)
+
+
+def run_prefill(args, ctx: Ctx, w: Workload) -> dict:
+    torch = ctx.torch
+    from warpforth_b200 import warpforth as wf
+    from warpforth_b200.sharded import ShardedPrefill
+
+    world, dev = ctx.world, ctx.dev
+    tdt = torch.bfloat16 if w.dtype == "bf16" else torch.float32
+    flush = w.S < 4096  # the [8,12,1024] inputs (50-100 MB) fit in L2; 1.6 GB do not
+    torch.manual_seed(w.seed)
+    sp = None
+    parity = None
+    if w.sharded:
+        q, k, v = (torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt) for _ in range(3))
+        sp = ShardedPrefill(w.B, w.H, w.S, w.D, dtype=tdt, device=dev,
+                            chunks=args.chunks or None, transport=args.transport)
+        qs, ks, vs = sp.shard(q), sp.shard(k), sp.shard(v)
+        units = prefill_flops(w)  # whole job per step
+        kernel_flops = prefill_flops(w, sp.local_heads)
+
+        def step():
+            # this rank's heads; the gather of O rides along (peer stores from the
+            # kernel, or per-chunk NCCL all-gathers overlapping compute)
+            sp(qs, ks, vs)
+
+        timed = step
+    else:
+        q, k, v = (torch.randn(w.B, w.H, w.S, w.D, device=dev).to(tdt) for _ in range(3))
+        out = torch.empty_like(q)
+        units = prefill_flops(w) * world  # every rank runs one replica
+        kernel_flops = prefill_flops(w)
+
+        def step():
+            wf.attention(q, k, v, out=out)
+
+        timed = None
+    for _ in range(args.warmup):
+        if flush:
+            ctx.flush_l2()
+        step()
+    if timed is None:
+        timed = graph_of(ctx, step).replay
+    total_ms, per, clock_info = time_steps(ctx, timed, args.steps, flush)
+    kernel_ms = statistics.mean(per)
+    if w.sharded:
+        # every rank recomputes the whole output on its own GPU with the same kernel and
+        # compares it bit for bit with the gathered one (all steps had these inputs)
+        got = sp.output_view()
+        ref = torch.empty((w.B, w.H, w.S, w.D), dtype=tdt, device=dev)
+        wf.attention_gather(q, k, v, [ref])
+        torch.cuda.synchronize()
+        exact = float(torch.equal(got, ref))
+        rel = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
+        parity = {"heads_checked": w.B * w.H, "bit_exact": ctx.min_over_ranks(exact) == 1.0,
+                  "max_rel_err": ctx.max_over_ranks(rel), "ranks_checked": world,
+                  "reference": "every rank: the same kernel for all heads on its own GPU"}
+        del ref, got
+        # the roofline's kernel time: this rank's heads alone, without the final barrier
+        ev = [(ctx.event(), ctx.event()) for _ in range(args.steps)]
+        for a, b in ev:
+            a.record(ctx.stream)
+            sp.compute_local(qs, ks, vs)
+            b.record(ctx.stream)
+        torch.cuda.synchronize()
+        kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+        ctx.barrier()
+    total_ms = ctx.max_over_ranks(total_ms)
+    kernel_ms = ctx.max_over_ranks(kernel_ms)
+    ms_per_step = total_ms / args.steps
+    value = units / (ms_per_step / 1e3) / 1e12
+
+    # ---------------- end to end through the public API with host buffers
+    steps = max(1, min(args.steps, args.e2e_steps))
+    g = torch.Generator().manual_seed(w.seed + 1000)
+    heads = sp.local_heads if sp is not None else w.H
+    shape = (w.B, heads, w.S, w.D)
+    host = [torch.randn(*shape, generator=g).to(tdt).pin_memory() for _ in range(3)]
+    dev_in = [torch.empty(shape, dtype=tdt, device=dev) for _ in range(3)]
+    if sp is not None:
+        host_out = torch.empty((w.B, w.H, w.S, w.D), dtype=tdt).pin_memory() \
+            if ctx.rank == 0 else None
+    else:
+        res = torch.empty(shape, dtype=tdt, device=dev)
+        host_out = torch.empty(shape, dtype=tdt).pin_memory()
+
+    def one():
+        for h_, d_ in zip(host, dev_in):
+            d_.copy_(h_, non_blocking=True)
+        if sp is not None:
+            out_ = sp(*(sp.split_local(t) for t in dev_in))
+            if host_out is not None:
+                host_out.copy_(out_, non_blocking=True)
+        else:
+            wf.attention(*dev_in, out=res)
+            host_out.copy_(res, non_blocking=True)
+
+    e2e_ms = timed_e2e(ctx, one, steps, args.warmup, flush)
+    e2e = {"value": units / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+           "steps": steps, "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
+           "d2h_bytes_per_step": host_out.numel() * host_out.element_size() if host_out is not None
+           else 0,
+           "path": "warpforth_b200.warpforth (ctypes) -> libwfattn C ABI, pinned host buffers"}
+    del host, dev_in
+
+    if w.dtype == "f32":
+        peak = f32_fma_peak(ctx.peaks)
+        roof = {"bound": "fp32-simt", "peak": peak, "peak_source": "nominal f32 FMA rate at max "
+                "SM clock", "kernel": "prefill_f32_kernel"}
+    else:
+        key = "bf16_tflops_sustained" if (w.sharded and ms_per_step > 1000) else "bf16_tflops"
+        roof = {"bound": "tensor", "peak": float(ctx.peaks[key]),
+                "peak_source": f"{ctx.peak_src} {key}",
+                "kernel": "prefill_bf16_2q_kernel" if (w.S + 255) // 256 * w.B * heads >= 148
+                else "prefill_bf16_kernel"}
+    achieved = kernel_flops / (kernel_ms / 1e3) / 1e12
+    traffic = load_traffic(w)
+    if traffic is not None and w.sharded:
+        traffic = int(traffic * heads / w.H)  # this rank's launch
+    roof.update({"achieved": achieved, "unit": "TFLOP/s", "frac": achieved / roof["peak"],
+                 "kernel_ms": kernel_ms, "traffic": traffic,
+                 "algorithmic_flop_per_launch": kernel_flops})
+    line = {
+        "metric": "causal SDPA TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "strong" if w.sharded else "weak",
+        "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+        "config": dict(config_of(w, world), **({"gather": sp.transport} if sp else {}),
+                       device_timing="per-rank CUDA events around each step, max over ranks"
+                       if w.sharded else "CUDA events around each step's library call, "
+                       "replayed from a CUDA graph"),
+        "roofline": roof, "e2e": e2e,
+        # kernels of this library per timed step, all ranks: one launch per head chunk
+        "gpu_launches": args.steps * world * (sp.chunks if sp is not None else 1),
+        "clocks": clock_info,
+    }
+    if parity is not None:
+        line["parity"] = parity
+    if not w.sharded and w.dtype == "f32" and ctx.rank == 0:
+        line["reference_ptx"] = ref_ptx_prefill(ctx, w, q, k, v, out, args)
+    if sp is not None:
+        sp.close()  # collective: unmaps and frees the peer output buffers
+    return line
+
+
+def run_decode(args, ctx: Ctx, w: Workload) -> dict:
+    torch = ctx.torch
+    from warpforth_b200 import warpforth as wf
+
+    dev, world = ctx.dev, ctx.world
+    tdt = torch.bfloat16
+    torch.manual_seed(w.seed)
+    lens = decode_lens().to(dev)
+    kc = torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt)
+    vc = torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt)
+    qd = torch.randn(w.B, w.H, w.D, device=dev, dtype=tdt)
+    od = torch.empty(w.B, w.H, w.D, device=dev, dtype=torch.float32)
+    ws = wf.DecodeWorkspace()
+    kv_bytes = int(decode_lens().sum()) * w.H * w.D * 2 * 2
+
+    def step():
+        wf.decode(qd, kc, vc, lens, out=od, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    # the 913 MB of K/V read per step exceed L2: no flush
+    total_ms, per, clock_info = time_steps(ctx, graph_of(ctx, step).replay, args.steps, False)
+    total_ms = ctx.max_over_ranks(total_ms)
+    # the roofline's kernel: the split kernel alone (the combine kernel reads 26 MB)
+    split_ms = ctx.max_over_ranks(statistics.mean(per))
+    ms_per_step = total_ms / args.steps
+    value = kv_bytes * world / (ms_per_step / 1e3) / 1e9
+
+    # end to end, decode serving: the KV cache is resident state; a step's inputs are the new
+    # query token, the new K/V row of every (batch, head) and the lengths
+    g = torch.Generator().manual_seed(w.seed + 1000)
+    q_h, knew_h, vnew_h = (torch.randn(w.B, w.H, w.D, generator=g).to(tdt).pin_memory()
+                           for _ in range(3))
+    lens_h = decode_lens().pin_memory()
+    qn, knew, vnew = (torch.empty((w.B, w.H, w.D), dtype=tdt, device=dev) for _ in range(3))
+    lens_d = torch.empty(w.B, dtype=torch.int32, device=dev)
+    out_h = torch.empty((w.B, w.H, w.D), dtype=torch.float32).pin_memory()
+    bidx = torch.arange(w.B, device=dev)
+
+    def one():
+        for h_, d_ in ((q_h, qn), (knew_h, knew), (vnew_h, vnew), (lens_h, lens_d)):
+            d_.copy_(h_, non_blocking=True)
+        pos = (lens_d - 1).long()
+        kc[bidx, :, pos] = knew
+        vc[bidx, :, pos] = vnew
+        wf.decode(qn, kc, vc, lens_d, out=od, workspace=ws)
+        out_h.copy_(od, non_blocking=True)
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    e2e_ms = timed_e2e(ctx, one, steps, args.warmup, False)
+    e2e = {"value": kv_bytes * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+           "ms_per_step": e2e_ms, "steps": steps,
+           "h2d_bytes_per_step": 3 * q_h.numel() * q_h.element_size() + lens_h.numel() * 4,
+           "d2h_bytes_per_step": out_h.numel() * 4,
+           "path": "warpforth_b200.warpforth.decode (ctypes) -> libwfattn C ABI; new K/V rows "
+                   "scattered into the resident cache"}
+    peak = float(ctx.peaks["hbm_gbs"])
+    achieved = kv_bytes / (split_ms / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": f"{ctx.peak_src} hbm_gbs",
+            "kernel": "decode_split_kernel + decode_combine_kernel (one library call)",
+            "kernel_ms": split_ms, "traffic": load_traffic(w),
+            "algorithmic_bytes_per_launch": kv_bytes}
+    return {
+        "metric": "decode attention KV GB/s per B200", "value": value, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": dict(config_of(w, world), device_timing="CUDA events "
+                                            "around each step's library call, replayed from a "
+                                            "CUDA graph"),
+        "roofline": roof, "e2e": e2e, "gpu_launches": args.steps * world * 2,
+        "clocks": clock_info,
+    }
+
+
+def run_head_call(args, ctx: Ctx, w: Workload) -> dict:
+    """Config 1: one [1,12,64,64] f32 attention call; latency per call."""
+    torch = ctx.torch
+    from warpforth_b200 import warpforth as wf
+
+    dev = ctx.dev
+    torch.manual_seed(w.seed)
+    q, k, v = (torch.randn(w.B, w.H, w.S, w.D).to(dev) for _ in range(3))
+    out = torch.empty_like(q)
+
+    def step():
+        wf.attention(q, k, v, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    n_calls = 100  # a step of ~10 us is timed as the mean of 100 graph-replayed calls
+    g = graph_of(ctx, step)
+    total_ms, per, clock_info = time_steps(ctx, lambda: [g.replay() for _ in range(n_calls)],
+                                           args.steps, False)
+    us = total_ms / args.steps / n_calls * 1e3
+    # end to end: copies in, the call through the reference-shaped ABI (12 launches of one
+    # head each, as demo/gpt2_generate.py:42-50 does), copy out
+    host = [t.cpu().pin_memory() for t in (q, k, v)]
+    host_out = torch.empty_like(host[0]).pin_memory()
+    kern = wf.AttentionKernel()
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+
+    def one():
+        for h_, d_ in zip(host, (dq, dk, dv)):
+            d_.copy_(h_, non_blocking=True)
+        for h in range(w.H):
+            kern(dq[0, h], dk[0, h], dv[0, h], out[0, h], w.S, w.D)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_ms = timed_e2e(ctx, one, 20, args.warmup, False)
+    flops = prefill_flops(w)
+    peak = f32_fma_peak(ctx.peaks)
+    achieved = flops / (us / 1e6) / 1e12
+    line = {
+        "metric": "GPT-2 attention call latency", "value": us, "unit": "us per call",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(config_of(w, 1), device_timing=f"CUDA events around {n_calls} graph "
+                       "replays of the batched library call per step"),
+        "roofline": {"bound": "latency (6.4 MFLOP per call: launch and fill dominate)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": "nominal f32 FMA rate at max SM "
+                     "clock", "kernel": "prefill_f32_kernel", "kernel_ms": us / 1e3,
+                     "traffic": None},
+        "e2e": {"value": e2e_ms * 1e3, "unit": "us per call", "ms_per_step": e2e_ms, "steps": 20,
+                "h2d_bytes_per_step": 3 * host[0].numel() * 4,
+                "d2h_bytes_per_step": host_out.numel() * 4,
+                "path": "AttentionKernel (the demo binding's interface): 12 one-head launches "
+                        "through wfattn_attention, pinned host buffers"},
+        "gpu_launches": args.steps * n_calls, "clocks": clock_info,
+    }
+    if ctx.rank == 0:
+        line["reference_ptx"] = ref_ptx_head_call(ctx, w, q, k, v, args)
+    return line
+
+
+def run_gpt2(args, ctx: Ctx, w: Workload) -> dict:
+    """GPT-2 generation tokens/s with every attention through libwfattn (one process per GPU)."""
+    torch = ctx.torch
+    from warpforth_b200 import gpt2
+
+    dev, world = ctx.dev, ctx.world
+    model = gpt2.random_gpt2(seed=1, device=dev)
+    prompt = gpt2.synthetic_prompt(32, seed=1)
+    prompt_dev = prompt.to(dev)
+    restore = gpt2.patch_gpt2()
+    steps = max(1, min(args.steps, args.gpt2_steps))
+    try:
+        for _ in range(args.warmup):
+            ids = gpt2.generate(model, prompt_dev, w.S, use_cache=w.use_cache)
+        torch.cuda.synchronize()
+        calls = gpt2.count_calls(lambda: gpt2.generate(model, prompt_dev, w.S,
+                                                       use_cache=w.use_cache))
+        total_ms, _, clock_info = time_steps(
+            ctx, lambda: gpt2.generate(model, prompt_dev, w.S, use_cache=w.use_cache), steps,
+            False)
+        ms = ctx.max_over_ranks(total_ms / steps)
+        value = w.S * world / (ms / 1e3)
+        # end to end: prompt from (pinned) host memory, ids read back, inside the timed region
+        host_prompt = prompt.pin_memory()
+
+        def one():
+            return gpt2.generate(model, host_prompt.to(dev, non_blocking=True), w.S,
+                                 use_cache=w.use_cache).cpu()
+
+        out = one()
+        e2e_ms = timed_e2e(ctx, one, min(steps, args.e2e_steps), 0, False)
+    finally:
+        restore()
+    assert ids.shape[1] == 32 + w.S and out.shape[1] == 32 + w.S
+    # the attention kernel of the step's largest prefill call, [1, 12, 159, 64] f32, alone
+    from warpforth_b200 import warpforth as wf
+
+    s_max = 32 + w.S - 1
+    q, k, v = (torch.randn(1, 12, s_max, 64, device=dev) for _ in range(3))
+    o = torch.empty_like(q)
+    kms = _ref_time(ctx, graph_of(ctx, lambda: wf.attention(q, k, v, out=o)).replay, 100)
+    kflops = 4 * 64 * 12 * (s_max * (s_max + 1) // 2)
+    peak = f32_fma_peak(ctx.peaks)
+    line = {
+        "metric": "GPT-2 gen tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights, random prompt ids)",
+        "config": dict(config_of(w, world), device_timing="CUDA events around whole "
+                       "generate() calls (host launch path included)"),
+        "roofline": {"bound": "launch/latency (attention is a small part of a GPT-2 step)",
+                     "kernel": f"prefill_f32_kernel at [1,12,{s_max},64]",
+                     "achieved": kflops / (kms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": kflops / (kms / 1e3) / 1e12 / peak, "kernel_ms": kms,
+                     "traffic": None, "peak_source": "nominal f32 FMA rate at max SM clock",
+                     "attention_calls_per_step": calls},
+        "e2e": {"value": w.S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "steps": min(steps, args.e2e_steps),
+                "h2d_bytes_per_step": prompt.numel() * prompt.element_size(),
+                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "path": "transformers generate -> patched eager_attention_forward -> libwfattn"},
+        # library launches per step: one per attention call (two for a decode call)
+        "gpu_launches": steps * world * sum(calls.values()) + steps * world * calls.get(
+            "decode", 0),
+        "clocks": clock_info,
+    }
+    if ctx.rank == 0 and not w.use_cache:
+        line["reference_ptx"] = ref_ptx_gpt2(ctx, w, model, prompt_dev, args)
+    return line
+
+
+# ------------------------------------------------------------------ the reference's compiled kernel
+def _ref_kernel():
+    from oracle import ref_ptx
+
+    if not ref_ptx.available():
+        return None, {"unavailable": "oracle/_ref/attention.ptx missing (make -C oracle ref "
+                                     "where the reference tree is present)"}
+    return ref_ptx.ReferencePtxKernel(), None
+
+
+def _ref_time(ctx: Ctx, fn, reps: int) -> float:
+    torch = ctx.torch
+    fn()
+    torch.cuda.synchronize()
+    a, b = ctx.event(), ctx.event()
+    a.record(ctx.stream)
+    for _ in range(reps):
+        fn()
+    b.record(ctx.stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def ref_ptx_prefill(ctx: Ctx, w: Workload, q, k, v, out, args) -> dict:
+    """The reference's compiled kernel on the same f32 inputs: one launch per (batch, head)
+    with grid = block = (S, 1, 1), as demo/gpt2_generate.py:42-50 launches it."""
+    import numpy as np
+
+    kern, bad = _ref_kernel()
+    if bad:
+        return bad
+    ro = ctx.torch.zeros_like(q)
+
+    def run():
+        for b in range(w.B):
+            for h in range(w.H):
+                kern(q[b, h], k[b, h], v[b, h], ro[b, h], w.S, w.D)
+
+    ms = _ref_time(ctx, run, max(1, min(args.steps, 5)))
+    err = float(np.abs(ro.cpu().numpy() - out.cpu().numpy()).max())
+    fl = prefill_flops(w)
+    return {"value": fl / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "launches_per_step": w.B * w.H, "max_abs_diff_vs_wfattn": err,
+            "what": "demo/attention.ptx (the reference's compiled kernel) via cuModuleLoadData "
+                    "+ cuLaunchKernel, one launch per head, timed with CUDA events"}
+
+
+def ref_ptx_head_call(ctx: Ctx, w: Workload, q, k, v, args) -> dict:
+    import numpy as np
+
+    kern, bad = _ref_kernel()
+    if bad:
+        return bad
+    ro = ctx.torch.zeros_like(q)
+
+    def run():
+        for h in range(w.H):
+            kern(q[0, h], k[0, h], v[0, h], ro[0, h], w.S, w.D)
+
+    ms = _ref_time(ctx, run, 50)
+    from warpforth_b200 import warpforth as wf
+
+    err = float(np.abs(ro.cpu().numpy() - wf.attention(q, k, v).cpu().numpy()).max())
+    return {"value": ms * 1e3, "unit": "us per call", "launches_per_step": w.H,
+            "max_abs_diff_vs_wfattn": err,
+            "what": "demo/attention.ptx, 12 one-head launches per call (the demo's loop), "
+                    "CUDA events over 50 calls"}
+
+
+def ref_ptx_gpt2(ctx: Ctx, w: Workload, model, prompt_dev, args) -> dict:
+    """The demo's own path: greedy generation with its per-head patch around the compiled
+    reference kernel (demo/gpt2_generate.py:25-54)."""
+    torch = ctx.torch
+    import transformers.models.gpt2.modeling_gpt2 as gpt2_module
+
+    from oracle import ref_ptx
+    from warpforth_b200 import gpt2
+
+    kern, bad = _ref_kernel()
+    if bad:
+        return bad
+    original = gpt2_module.eager_attention_forward
+    gpt2_module.eager_attention_forward = ref_ptx.make_reference_eager_attn(kern)
+    try:
+        ids = gpt2.generate(model, prompt_dev, w.S)
+        torch.cuda.synchronize()
+        a, b = ctx.event(), ctx.event()
+        a.record(ctx.stream)
+        ids = gpt2.generate(model, prompt_dev, w.S)
+        b.record(ctx.stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+    finally:
+        gpt2_module.eager_attention_forward = original
+    restore = gpt2.patch_gpt2()
+    try:
+        ours = gpt2.generate(model, prompt_dev, w.S)
+    finally:
+        restore()
+    return {"value": w.S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "tokens_match_wfattn": bool(torch.equal(ids, ours)),
+            "what": "the demo's patch (contiguous copies, zeroed output, one launch per head of "
+                    "batch 0) around demo/attention.ptx; one timed generation after one warm-up"}
+
+
+# ------------------------------------------------------------------ composition
+RUNNERS = {"prefill": run_prefill, "decode": run_decode, "gpt2": run_gpt2,
+           "head_call": run_head_call}
+
+
+def summarise_side(line: dict) -> dict:
+    keep = ("metric", "value", "unit", "higher_is_better", "ms_per_step", "steps", "warmup",
+            "dtype", "config", "roofline", "e2e", "cpu_baseline", "clocks", "gpu_launches",
+            "reference_ptx", "parity")
+    return {k: line[k] for k in keep if k in line}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -291,12 +1026,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["wfattn", "reference"], default="wfattn")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="long_prefill")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0,
-                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=6.0,
+                    help="target CPU time of each cpu_baseline sample")
     ap.add_argument("--ref-step-seconds", type=float, default=4.0,
                     help="target CPU time of one reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side", action="store_true",
+                    help="measure the chosen workload only (no `workloads` object)")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--gpt2-steps", type=int, default=3,
+                    help="timed generations of the GPT-2 workloads (at most --steps)")
     ap.add_argument("--shape", default=None,
                     help="B,H,S override of a prefill workload (profiling a smaller case)")
     ap.add_argument("--transport", choices=["auto", "peer", "nccl"], default="auto",
@@ -313,478 +1052,35 @@ def main() -> None:
         b, h, s = (int(x) for x in args.shape.split(","))
         if w.kind != "prefill":
             ap.error("--shape applies to prefill workloads only")
-        w = Workload(w.name, w.kind, b, h, s, w.D, w.seed, w.dtype, w.sharded,
-                     f"causal prefill [{b},{h},{s},{w.D}] {w.dtype} (shape override of "
-                     f"{w.name})")
+        w = replace(w, B=b, H=h, S=s, description=f"causal prefill [{b},{h},{s},{w.D}] "
+                    f"{w.dtype} (shape override of {w.name})")
     if args.impl == "reference":
         run_reference(args, w)
         return
-    if w.kind == "gpt2":
-        run_gpt2(args, w)
-        return
-    run_gpu(args, w)
-
-
-def gpt2_cpu_sample(target_s: float, threads: int) -> dict:
-    """Stock eager GPT-2 on the host cores (the demo's torch attention), greedy tokens/s."""
-    import torch
-
-    from warpforth_b200 import gpt2
-
-    torch.set_num_threads(threads)
-    model = gpt2.random_gpt2(seed=1, device="cpu")
-    prompt = gpt2.synthetic_prompt(32, seed=1)
-    n = 4
-    while True:
-        t0 = time.perf_counter()
-        gpt2.generate(model, prompt, n, use_cache=False)
-        dt = time.perf_counter() - t0
-        if dt >= 0.5 * target_s or n >= 128:
-            break
-        n = min(128, max(n + 1, int(n * min(8.0, target_s / max(dt, 1e-3)))))
-    return {"value": n / dt, "unit": "tokens/s", "seconds": dt,
-            "sample": f"stock eager GPT-2 (torch CPU, {threads} threads): the first {n} greedy "
-                      f"tokens of the same prompt in {dt:.2f} s"}
-
-
-def run_gpt2(args, w: Workload) -> None:
-    """GPT-2 generation tokens/s with every attention through libwfattn (one process per GPU)."""
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    from warpforth_b200 import gpt2
-
-    model = gpt2.random_gpt2(seed=1, device=dev)
-    prompt = gpt2.synthetic_prompt(32, seed=1)
-    prompt_dev = prompt.to(dev)
-    restore = gpt2.patch_gpt2()
-    stream = torch.cuda.current_stream(dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    for _ in range(args.warmup):
-        gpt2.generate(model, prompt_dev, w.S)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = ClockSampler(physical_gpu_indices(world)) if rank == 0 else None
-    if clocks:
-        clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        ids = gpt2.generate(model, prompt_dev, w.S)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clock_info = clocks.stop() if clocks else None
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-    assert ids.shape[1] == 32 + w.S
-    value = w.S * world / (ms / 1e3)
-
-    # end to end: prompt from (pinned) host memory, ids read back, inside the timed region
-    host_prompt = prompt.pin_memory()
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        out = gpt2.generate(model, host_prompt.to(dev, non_blocking=True), w.S).cpu()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    restore()
-
-    # the attention kernel at the step's largest call, [1, 12, 159, 64] f32, on its own
-    from warpforth_b200 import warpforth as wf
-
-    s_max = 32 + w.S - 1
-    q, k, v = (torch.randn(1, 12, s_max, 64, device=dev) for _ in range(3))
-    o = torch.empty_like(q)
-    for _ in range(10):
-        wf.attention(q, k, v, out=o)
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    for _ in range(100):
-        wf.attention(q, k, v, out=o)
-    a1.record(stream)
-    torch.cuda.synchronize()
-    kms = a0.elapsed_time(a1) / 100
-    kflops = 4 * 64 * 12 * (s_max * (s_max + 1) // 2)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = gpt2_cpu_sample(args.cpu_seconds, os.cpu_count() or 1)
-        cpu = {"value": r["value"], "unit": r["unit"], "cores": os.cpu_count(),
-               "kind": "port", "sample": r["sample"]}
-    if rank == 0:
-        peak = 148 * 128 * 2 * 1965e6 / 1e12
-        achieved = kflops / (kms / 1e3) / 1e12
-        line = {
-            "metric": "GPT-2 gen tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (random-init weights, random prompt ids)",
-            "config": config_of(w, world),
-            "roofline": {"bound": "launch/latency (attention is a small part of a GPT-2 step)",
-                         "kernel": "prefill_f32_kernel at [1,12,159,64]",
-                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "kernel_ms": kms, "traffic": None,
-                         "peak_source": "nominal f32 FMA rate at max SM clock"},
-            "cpu_baseline": cpu,
-            "e2e": {"value": w.S * world / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "ms_per_step": e2e_ms, "steps": e2e_steps,
-                    "h2d_bytes_per_step": prompt.numel() * prompt.element_size(),
-                    "d2h_bytes_per_step": out.numel() * out.element_size(),
-                    "path": "transformers generate -> patched eager_attention_forward -> "
-                            "libwfattn"},
-            "gpu_launches": args.steps * world * 12 * w.S,
-            "clocks": clock_info,
-        }
+    ctx = Ctx()
+    if ctx.world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ctx.world}")
+    line = RUNNERS[w.kind](args, ctx, w)
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_of(w, args.cpu_seconds)
+    side = {}
+    if (ctx.world == 1 and not args.no_side and not args.shape
+            and args.workload == "long_prefill"):
+        for name in SIDE_WORKLOADS:
+            sw = WORKLOADS[name]
+            ctx.torch.cuda.empty_cache()
+            try:
+                sub = RUNNERS[sw.kind](args, ctx, sw)
+                if not args.no_cpu_baseline:
+                    sub["cpu_baseline"] = cpu_baseline_of(sw, args.cpu_seconds)
+                side[name] = summarise_side(sub)
+            except Exception as e:  # a side workload never hides the headline line
+                side[name] = {"error": f"{type(e).__name__}: {e}"}
+    if side:
+        line["workloads"] = side
+    if ctx.rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def run_gpu(args, w: Workload) -> None:
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
-    from warpforth_b200 import warpforth as wf
-    from warpforth_b200.sharded import ShardedPrefill
-
-    peaks, peak_src = load_peaks()
-    stream = torch.cuda.current_stream(dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    # A step whose inputs exceed L2 (126 MB) needs no flush: long prefill and
-    # decode (913 MB of K/V per step).  A flush by writes would also leave L2
-    # full of dirty lines whose write-back the next step would pay for.
-    needs_flush = w.kind == "prefill" and w.S < 4096
-
-    # ---------------- inputs (identical on every rank) and the step
-    tdt = torch.bfloat16 if w.dtype == "bf16" else torch.float32
-    torch.manual_seed(w.seed)
-    sp = None
-    if w.kind == "prefill":
-        if w.sharded:
-            q, k, v = (torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt) for _ in range(3))
-            sp = ShardedPrefill(w.B, w.H, w.S, w.D, dtype=tdt, device=dev,
-                                chunks=args.chunks or None, transport=args.transport)
-            qs, ks, vs = sp.shard(q), sp.shard(k), sp.shard(v)
-            local_heads = sp.local_heads
-            units = prefill_flops(w)  # whole job per step
-            kernel_flops = prefill_flops(w, local_heads)
-
-            def compute():
-                # this rank's heads; the gather of O rides along (peer stores from
-                # the kernel, or per-chunk NCCL all-gathers overlapping compute)
-                sp(qs, ks, vs)
-
-            def collective():
-                pass
-
-            def kernel_only():
-                sp.compute_local(qs, ks, vs)
-        else:
-            q, k, v = (torch.randn(w.B, w.H, w.S, w.D, device=dev).to(tdt) for _ in range(3))
-            out = torch.empty_like(q)
-            units = prefill_flops(w) * world  # every rank runs one replica
-            kernel_flops = prefill_flops(w)
-
-            def compute():
-                wf.attention(q, k, v, out=out)
-
-            def collective():
-                pass
-        unit_scale = 1e12
-    else:
-        lens = decode_lens().to(dev)
-        kc = torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt)
-        vc = torch.randn(w.B, w.H, w.S, w.D, device=dev, dtype=tdt)
-        qd = torch.randn(w.B, w.H, w.D, device=dev, dtype=tdt)
-        od = torch.empty(w.B, w.H, w.D, device=dev, dtype=torch.float32)
-        ws = wf.DecodeWorkspace()
-        kv_bytes = int(decode_lens().sum()) * w.H * w.D * 2 * 2
-        units = kv_bytes * world
-        kernel_flops = kv_bytes
-
-        def compute():
-            wf.decode(qd, kc, vc, lens, out=od, workspace=ws)
-
-        def collective():
-            pass
-        unit_scale = 1e9
-
-    def step():
-        compute()
-        collective()
-
-    # ---------------- device-timed loop
-    for _ in range(args.warmup):
-        if needs_flush:
-            flush.zero_()
-        step()
-    torch.cuda.synchronize()
-    timed_compute = compute
-    if not w.sharded:
-        # The step's library call (its kernel launches) captured once and
-        # replayed, so the device timing holds the GPU work and not the
-        # Python/ctypes launch path; `e2e` below goes through that path.
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            compute()
-        torch.cuda.synchronize()
-        timed_compute = graph.replay
-    barrier()
-    clocks = ClockSampler(physical_gpu_indices(world)) if rank == 0 else None
-    if clocks:
-        clocks.start()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    total_ms = 0.0
-    torch.cuda.synchronize()
-    barrier()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    if needs_flush:
-        # flush between steps; steps are timed individually and summed
-        for i in range(args.steps):
-            flush.zero_()
-            kev[i][0].record(stream)
-            timed_compute()
-            kev[i][1].record(stream)
-            collective()
-        torch.cuda.synchronize()
-        per_step = []
-        for i in range(args.steps):
-            per_step.append(kev[i][0].elapsed_time(kev[i][1]))
-        total_ms = sum(per_step)
-    else:
-        t_start.record(stream)
-        for i in range(args.steps):
-            kev[i][0].record(stream)
-            timed_compute()
-            kev[i][1].record(stream)
-            collective()
-        t_end.record(stream)
-        torch.cuda.synchronize()
-        total_ms = t_start.elapsed_time(t_end)
-    barrier()
-    clock_info = clocks.stop() if clocks else None
-    kernel_ms = statistics.mean(kev[i][0].elapsed_time(kev[i][1]) for i in range(args.steps))
-    if w.sharded:
-        # The timed steps overlap each chunk's all-gather with the next chunk's
-        # compute; the roofline's kernel time comes from the kernels alone.
-        for i in range(args.steps):
-            kev[i][0].record(stream)
-            kernel_only()
-            kev[i][1].record(stream)
-        torch.cuda.synchronize()
-        kernel_ms = statistics.mean(kev[i][0].elapsed_time(kev[i][1]) for i in range(args.steps))
-        barrier()
-    total_ms = max_over_ranks(total_ms)
-    kernel_ms_max = max_over_ranks(kernel_ms)
-    ms_per_step = total_ms / args.steps
-    value = units / (ms_per_step / 1e3) / unit_scale
-
-    # ---------------- end-to-end through the public API with host buffers
-    e2e = run_e2e(args, w, world, rank, dev, tdt, barrier, max_over_ranks, wf, sp, units,
-                  unit_scale, flush if needs_flush else None)
-
-    # ---------------- CPU baseline (rank 0, N=1 only)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import oracle
-
-        threads = host_threads()
-        r = cpu_sample(w, args.cpu_seconds, threads)
-        cpu = {"value": r["value"], "unit": r["unit"], "cores": threads, "kind": "port",
-               "sample": r["sample"]}
-
-    if rank == 0:
-        metric, unit, hib = metric_of(w)
-        if w.kind == "prefill":
-            peak_key = "bf16_tflops_sustained" if (w.sharded and ms_per_step > 1000) else \
-                "bf16_tflops"
-            achieved = kernel_flops / (kernel_ms_max / 1e3) / 1e12
-            if w.dtype == "f32":
-                # CUDA-core f32 FMA peak: 148 SMs x 128 lanes x 2 FLOP x max SM clock
-                peak = 148 * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
-                roof = {"bound": "fp32-simt", "achieved": achieved, "peak": peak,
-                        "unit": "TFLOP/s", "frac": achieved / peak,
-                        "peak_source": "nominal f32 FMA rate at max SM clock"}
-            else:
-                peak = float(peaks[peak_key])
-                roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                        "frac": achieved / peak, "peak_source": f"{peak_src} {peak_key}"}
-        else:
-            achieved = kernel_flops / (kernel_ms_max / 1e3) / 1e9
-            peak = float(peaks["hbm_gbs"])
-            roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs"}
-        traffic = load_traffic(w)
-        if traffic is not None and w.sharded:
-            traffic = int(traffic * local_heads / w.H)  # this rank's launch
-        roof["traffic"] = traffic
-        roof["kernel_ms"] = kernel_ms_max
-        line = {
-            "metric": metric, "value": value, "unit": unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": hib,
-            "scaling": "strong" if w.sharded else "weak",
-            "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
-            "config": dict(config_of(w, world), **({"gather": sp.transport} if sp else {}),
-                           device_timing=(
-                "per-rank CUDA events around each step" if w.sharded else
-                "CUDA events around each step's library call, replayed from a CUDA graph")),
-            "roofline": roof,
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            # kernels of this library per timed step, all ranks: decode = split + combine,
-            # sharded prefill = one launch per head chunk, otherwise one launch
-            "gpu_launches": args.steps * world * (2 if w.kind == "decode" else
-                                                  (sp.chunks if sp is not None else 1)),
-            "clocks": clock_info,
-        }
-        print(json.dumps(line), flush=True)
-    if sp is not None:
-        sp.close()  # collective: unmaps and frees the peer output buffers
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def run_e2e(args, w, world, rank, dev, tdt, barrier, max_over_ranks, wf, sp, units, unit_scale,
-            flush):
-    import torch
-
-    stream = torch.cuda.current_stream(dev)
-    steps = max(1, min(args.steps, args.e2e_steps))
-    g = torch.Generator().manual_seed(w.seed + 1000)
-    if w.kind == "prefill":
-        heads = sp.local_heads if sp is not None else w.H
-        shape = (w.B, heads, w.S, w.D)
-        host = [torch.randn(*shape, generator=g).to(tdt).pin_memory() for _ in range(3)]
-        dev_in = [torch.empty(shape, dtype=tdt, device=dev) for _ in range(3)]
-        if sp is not None:
-            res = sp.output_view()
-            host_out = torch.empty(tuple(res.shape), dtype=tdt).pin_memory() if rank == 0 else None
-        else:
-            res = torch.empty(shape, dtype=tdt, device=dev)
-            host_out = torch.empty(shape, dtype=tdt).pin_memory()
-
-        def one():
-            for h_, d_ in zip(host, dev_in):
-                d_.copy_(h_, non_blocking=True)
-            if sp is not None:
-                sp(*(sp.split_local(t) for t in dev_in))
-                if host_out is not None:
-                    host_out.copy_(sp.output_view(), non_blocking=True)
-            else:
-                wf.attention(*dev_in, out=res)
-                host_out.copy_(res, non_blocking=True)
-
-        h2d = sum(t.numel() * t.element_size() for t in host)
-        d2h = host_out.numel() * host_out.element_size() if host_out is not None else 0
-    else:
-        # Decode serving: the KV cache is resident state; a step's inputs are the
-        # new query token, the new K/V row of every (batch, head) and the lengths.
-        lens_d = decode_lens().to(dev)
-        shape = (w.B, w.H, w.S, w.D)
-        kc = torch.randn(*shape, device=dev, dtype=tdt)
-        vc = torch.randn(*shape, device=dev, dtype=tdt)
-        q_h, knew_h, vnew_h = (torch.randn(w.B, w.H, w.D, generator=g).to(tdt).pin_memory()
-                               for _ in range(3))
-        lens_h = decode_lens().pin_memory()
-        qd, knew, vnew = (torch.empty((w.B, w.H, w.D), dtype=tdt, device=dev) for _ in range(3))
-        lens = torch.empty(w.B, dtype=torch.int32, device=dev)
-        od = torch.empty((w.B, w.H, w.D), dtype=torch.float32, device=dev)
-        out_h = torch.empty((w.B, w.H, w.D), dtype=torch.float32).pin_memory()
-        ws = wf.DecodeWorkspace()
-        bidx = torch.arange(w.B, device=dev)
-
-        def one():
-            for h_, d_ in ((q_h, qd), (knew_h, knew), (vnew_h, vnew), (lens_h, lens)):
-                d_.copy_(h_, non_blocking=True)
-            pos = (lens - 1).long()
-            kc[bidx, :, pos] = knew
-            vc[bidx, :, pos] = vnew
-            wf.decode(qd, kc, vc, lens, out=od, workspace=ws)
-            out_h.copy_(od, non_blocking=True)
-
-        h2d = 3 * q_h.numel() * q_h.element_size() + lens_h.numel() * 4
-        d2h = out_h.numel() * 4
-        del lens_d
-    for _ in range(args.warmup):
-        one()
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    tot = 0.0
-    for _ in range(steps):
-        if flush is not None:
-            flush.zero_()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        one()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        tot += e0.elapsed_time(e1)
-    barrier()
-    ms = max_over_ranks(tot / steps)
-    return {"value": units / (ms / 1e3) / unit_scale, "unit": "TFLOP/s" if w.kind == "prefill"
-            else "GB/s", "ms_per_step": ms, "steps": steps,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "path": "warpforth_b200.warpforth (ctypes) -> libwfattn C ABI, pinned host buffers"}
-
-
-def host_threads() -> int:
-    """Host cores this process may run on.  torchrun sets OMP_NUM_THREADS=1 for every rank, so
-    the CPU legs pass their thread count explicitly instead of taking OpenMP's default."""
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+    ctx.close()
 
 
 def load_traffic(w: Workload):

@@ -117,12 +117,12 @@ WFATTN_API wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t head
  * rank's heads inside every rank's full output buffer when the buffers are
  * mapped across GPUs (wfattn_peer_alloc / wfattn_peer_open).  q, k, v and
  * outputs[0] must be device memory of the calling GPU (WFATTN_INVALID_ARG
- * otherwise): they are read and written by TMA; outputs[1..] receive plain
- * 16-byte stores from the kernel (no TMA touches another GPU's memory).
- * Every finished output tile goes to all of them as the kernel runs, so the
- * transfer overlaps the computation.  The
- * stores are complete when the kernel is; a caller that writes into other
- * GPUs' buffers synchronises with those GPUs afterwards.
+ * otherwise): they are read and written through TMA tensor maps.
+ * outputs[1..] receive untiled bulk copies (cp.async.bulk, shared -> global,
+ * no multicast) of every finished 32-row output slab, so the TMA engine moves
+ * the bytes over NVLink while the kernel computes the next tile.  The copies
+ * are complete when the kernel is; a caller that writes into other GPUs'
+ * buffers synchronises with those GPUs afterwards.
  */
 WFATTN_API wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_q,
                                                  int64_t seq_k, int64_t head_dim, const void *q,
@@ -163,6 +163,32 @@ WFATTN_API wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t h
                               const int64_t *v_strides, const int32_t *kv_lens, float *o,
                               const int64_t *o_strides, float scale, void *workspace,
                               size_t workspace_bytes, void *stream);
+
+/*
+ * Decode over an f32 KV cache: the same split-KV decode as wfattn_decode with
+ * f32 q, k_cache and v_cache (f32 arithmetic throughout, the f32 path's
+ * accuracy contract: <= 1e-5 absolute of the f64 reference).
+ *
+ * Replaces: nothing in the reference (no KV cache, demo/README.md:45); this is
+ * the decode step of the f32 GPT-2 demo run with use_cache=True, the cache
+ * being the f32 [B, H, L, D] keys and values the model keeps.
+ *
+ * Arguments as wfattn_decode, with these differences: q, k_cache, v_cache are
+ * f32; their strides must be multiples of 4 elements; the workspace needs
+ * wfattn_decode_f32_workspace_size() bytes (keys are split into 128-key
+ * chunks instead of 256).
+ */
+WFATTN_API size_t wfattn_decode_f32_workspace_size(int64_t batch, int64_t heads,
+                                                   int64_t max_kv_len, int64_t head_dim);
+
+WFATTN_API wfattn_status_t wfattn_decode_f32(int64_t batch, int64_t heads, int64_t head_dim,
+                                             int64_t max_kv_len, const float *q,
+                                             const int64_t *q_strides, const float *k_cache,
+                                             const int64_t *k_strides, const float *v_cache,
+                                             const int64_t *v_strides, const int32_t *kv_lens,
+                                             float *o, const int64_t *o_strides, float scale,
+                                             void *workspace, size_t workspace_bytes,
+                                             void *stream);
 
 /*
  * Decode without any device allocation -- no counterpart in the reference.

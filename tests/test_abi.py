@@ -159,3 +159,15 @@ def test_decode_shape_bounds_are_checked_without_overflow():
                                        None, 0.0, None)
         assert st == _lib.INVALID_ARG
         assert b"2^31-1" in lib.wfattn_last_error()
+
+
+def test_f32_decode_workspace_is_sized_for_128_key_chunks():
+    lib = _lib.load()
+    # 128-key chunks for an f32 cache: twice the partials of the bf16 decode's 256-key chunks
+    assert lib.wfattn_decode_f32_workspace_size(64, 25, 4096, 64) == 64 * 25 * 32 * 66 * 4
+    assert lib.wfattn_decode_f32_workspace_size(1, 12, 159, 64) == 12 * 2 * 66 * 4
+    assert lib.wfattn_decode_f32_workspace_size(1 << 40, 1 << 40, 4096, 64) == 0
+    st = lib.wfattn_decode_f32(1, 1, 64, 64, 16, None, 16, None, 16, None, 16, 16, None, 0.0,
+                               16, 100, None)
+    assert st == _lib.INVALID_ARG  # workspace too small: rejected on the host
+    assert b"workspace" in lib.wfattn_last_error()

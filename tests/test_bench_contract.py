@@ -55,7 +55,8 @@ def test_every_workload_has_a_metric_and_traffic_parses():
 
     for name, w in bench.WORKLOADS.items():
         metric, unit, hib = bench.metric_of(w)
-        assert metric and unit and hib is True
+        assert metric and unit
+        assert hib is (w.kind != "head_call")  # latency: lower is better
         assert bench.config_of(w, 1)["workload"]
     rows = [ln for ln in (ROOT / "profiles" / "traffic.md").read_text().splitlines()
             if ln.startswith("| ") and not ln.startswith("| workload") and "---" not in ln]
@@ -64,3 +65,13 @@ def test_every_workload_has_a_metric_and_traffic_parses():
         name = row.strip("|").split("|")[0].strip()
         assert name in bench.WORKLOADS, name
         assert bench.load_traffic(bench.WORKLOADS[name]) > 0
+
+
+def test_side_workloads_are_known_and_the_default_is_the_headline():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    assert all(name in bench.WORKLOADS for name in bench.SIDE_WORKLOADS)
+    assert "long_prefill" not in bench.SIDE_WORKLOADS
+    kinds = {bench.WORKLOADS[n].kind for n in bench.SIDE_WORKLOADS}
+    assert kinds <= set(bench.RUNNERS)

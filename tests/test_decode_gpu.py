@@ -121,3 +121,61 @@ def test_decode_bad_length_is_reported(wf):
     with pytest.raises(_lib.WfattnError, match="kv_lens"):
         wf.device_status(clear=True)
     wf.device_status(clear=True)  # cleared
+
+
+# ---------------------------------------------------------------- f32 cache (wfattn_decode_f32)
+F32_ABS_TOL = 1e-5
+
+
+def _case_f32(b, h, lmax, lens, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, h, 64, generator=g)
+    kc = torch.randn(b, h, lmax, 64, generator=g)
+    vc = torch.randn(b, h, lmax, 64, generator=g)
+    return q, kc, vc, torch.tensor(lens, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("lens", [[1], [2], [127], [128], [129], [255, 256, 257, 1000],
+                                  [1, 4096, 17, 3000], [32, 159]])
+def test_decode_f32_ragged_lengths_at_the_f32_contract(wf, lens):
+    # 128-key chunks: lengths around one and two chunks, a long and a 1-key sequence
+    q, kc, vc, kl = _case_f32(len(lens), 3, max(lens), lens, 21)
+    out = wf.decode(q.cuda(), kc.cuda(), vc.cuda(), kl.cuda()).cpu().numpy()
+    assert np.isfinite(out).all()
+    assert np.abs(out - _ref(q, kc, vc, kl)).max() <= F32_ABS_TOL
+
+
+def test_decode_f32_strided_query_scale_padding_and_gpt2_layout(wf):
+    # q as the [B, H, 1, D] view of a [B, 1, H, D] projection (GPT-2's layout), NaN in the
+    # cache padding, an explicit scale, and a workspace reused across calls
+    q, kc, vc, kl = _case_f32(2, 12, 300, [159, 300], 22)
+    qv = q[:, None].contiguous().transpose(1, 2)  # [B, H, 1, D] with strides (H*D, D, H*D, 1)
+    kcn, vcn = kc.clone(), vc.clone()
+    kcn[0, :, 159:] = float("nan")
+    vcn[0, :, 159:] = float("nan")
+    ws = wf.DecodeWorkspace()
+    for scale in (None, 0.125, 0.3):
+        out = wf.decode(qv.cuda(), kcn.cuda(), vcn.cuda(), kl.cuda(), scale=scale,
+                        workspace=ws).cpu().numpy()
+        assert np.isfinite(out).all()
+        assert np.abs(out - _ref(q, kc, vc, kl, scale=scale)).max() <= F32_ABS_TOL
+
+
+def test_decode_f32_config4_shape(wf):
+    # config 4's lengths and shape with an f32 cache (every sequence against the oracle)
+    lens = torch.randint(512, 4097, (64,), generator=torch.Generator().manual_seed(3),
+                         dtype=torch.int64).to(torch.int32)
+    torch.manual_seed(3)
+    kc = torch.randn(64, 25, 4096, 64)
+    vc = torch.randn(64, 25, 4096, 64)
+    q = torch.randn(64, 25, 64)
+    out = wf.decode(q.cuda(), kc.cuda(), vc.cuda(), lens.cuda()).cpu().numpy()
+    assert np.isfinite(out).all()
+    assert np.abs(out - _ref(q, kc, vc, lens)).max() <= F32_ABS_TOL
+    wf.device_status(clear=True)
+
+
+def test_decode_rejects_mixed_dtypes(wf):
+    q, kc, vc, kl = _case_f32(1, 1, 8, [8], 23)
+    with pytest.raises(ValueError, match="all bfloat16 or all float32"):
+        wf.decode(q.cuda(), kc.cuda().bfloat16(), vc.cuda(), kl.cuda())

@@ -1,9 +1,9 @@
 """GPT-2 end to end with every attention routed through libwfattn (the demo's caller).
 
 Random-init GPT-2 small (seed 1), a 32-token prompt (seed 1), greedy
-generation with use_cache=False as in demo/gpt2_generate.py:80-90.  The
-patched model must produce the same token ids as the stock eager model on the
-GPU and on the CPU; a difference is only accepted where the stock model's top
+generation with use_cache=False as in demo/gpt2_generate.py:80-90, and with
+the KV cache through the decode kernel.  The patched model must produce the
+same token ids as the stock eager model on the GPU and on the CPU; a difference is only accepted where the stock model's top
 two logits are within 1e-4 (a genuine tie that f32 rounding may break either
 way).
 """
@@ -59,15 +59,23 @@ def test_gpt2_generation_matches_stock_eager(gpt2):
     assert float((lp - ls).abs().max()) <= 1e-3
 
 
-def test_gpt2_generation_with_kv_cache(gpt2):
+def test_gpt2_generation_with_kv_cache_through_the_decode_kernel(gpt2):
+    # use_cache=True (not supported by the reference demo): the prompt goes through the
+    # prefill kernel once per layer, each of the 127 later tokens through the f32 decode
+    # kernel once per layer
     model = gpt2.random_gpt2(seed=1, device="cuda")
     prompt = gpt2.synthetic_prompt(32, seed=1)
-    stock = gpt2.generate(model, prompt, 64, use_cache=True)
+    stock = gpt2.generate(model, prompt, 128, use_cache=True)
     restore = gpt2.patch_gpt2()
     try:
-        patched = gpt2.generate(model, prompt, 64, use_cache=True)
+        out = {}
+        calls = gpt2.count_calls(lambda: out.setdefault(
+            "ids", gpt2.generate(model, prompt, 128, use_cache=True)))
     finally:
         restore()
+    patched = out["ids"]
+    assert patched.shape[1] == 32 + 128
+    assert calls == {"prefill": 12, "decode": 12 * 127}
     _assert_same_or_tie(model, stock, patched, 32)
 
 

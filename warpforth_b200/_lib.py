@@ -20,7 +20,7 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 EXPORTED_SYMBOLS = (
     "wfattn_version", "wfattn_status_string", "wfattn_last_error", "wfattn_attention",
     "wfattn_prefill", "wfattn_prefill_gather", "wfattn_decode_workspace_size", "wfattn_decode",
-    "wfattn_decode_noalloc", "wfattn_device_status", "wfattn_peer_alloc", "wfattn_peer_open",
+    "wfattn_decode_f32_workspace_size", "wfattn_decode_f32", "wfattn_decode_noalloc", "wfattn_device_status", "wfattn_peer_alloc", "wfattn_peer_open",
     "wfattn_peer_close", "wfattn_peer_free",
 )
 
@@ -77,6 +77,10 @@ def load() -> ctypes.CDLL:
     lib.wfattn_decode.restype = ctypes.c_int
     lib.wfattn_decode.argtypes = [_i64, _i64, _i64, _i64, _vp, _i64p, _vp, _i64p, _vp, _i64p,
                                   _vp, _vp, _i64p, ctypes.c_float, _vp, ctypes.c_size_t, _vp]
+    lib.wfattn_decode_f32_workspace_size.restype = ctypes.c_size_t
+    lib.wfattn_decode_f32_workspace_size.argtypes = [_i64, _i64, _i64, _i64]
+    lib.wfattn_decode_f32.restype = ctypes.c_int
+    lib.wfattn_decode_f32.argtypes = lib.wfattn_decode.argtypes
     lib.wfattn_decode_noalloc.restype = ctypes.c_int
     lib.wfattn_decode_noalloc.argtypes = [_i64, _i64, _i64, _i64, _vp, _i64p, _vp, _i64p, _vp,
                                           _i64p, _vp, _vp, _i64p, ctypes.c_float, _vp]

@@ -22,11 +22,12 @@
 //                     32*(w%4)..+31, the sub-partition it may access): the
 //                     row max and row sum need no shuffles and each thread
 //                     packs its own P row.  At the end of an item each warp
-//                     writes its 32 output rows to a swizzled staging slab
-//                     and one TMA store into the local output; for a fused
-//                     all-gather the same warp copies the slab to every
-//                     further destination (other GPUs' buffers) with plain
-//                     16-byte stores.
+//                     writes its 32 output rows to a staging slab and one
+//                     TMA store into the local output; for a fused all-gather
+//                     the same lane queues bulk copies of the slab to every
+//                     further destination (other GPUs' buffers), so the TMA
+//                     engine, not the softmax warp, moves those bytes over
+//                     NVLink while the next item computes.
 //
 // TMEM (512 columns): S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384)
 //                     O_A [384,448) O_B [448,512).
@@ -73,8 +74,9 @@ struct Smem {
   uint8_t q[2][2][kTileBytes];  // [slot][tile A/B]: Q of two consecutive work items
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  // Output staging, one 32-row x 128-byte slab per softmax warp in the TMA
-  // 128-byte-swizzle layout (16-byte chunk c of row r at c ^ (r % 8)).
+  // Output staging, one 32-row x 128-byte slab per softmax warp, row-major
+  // (row r at r * 128): a TMA tensor store (no swizzle) reads it for the local
+  // output and untiled bulk copies for the further destinations.
   uint8_t ostage[kSoftmaxWarps][32 * 128];
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
@@ -95,7 +97,7 @@ struct Params {
   int64_t n_items;  // n_pairs * B * H
   uint32_t group;   // consecutive blocks of one (batch, head) in the item order
   // Further destinations of the output (e.g. other GPUs' buffers mapped into
-  // this one), written with plain 16-byte stores; strides os_* are shared.
+  // this one), written by untiled bulk copies; strides os_* are shared.
   char *remote[kMaxOutputPeers - 1];
   int n_remote;
   int64_t os_b, os_h, os_s;
@@ -566,8 +568,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // ---- output of this item: O_t / l once the last P.V has completed.
       // O_t is handed back to the P.V thread as soon as it is in registers;
-      // the rows go out through this warp's staging slab and one TMA store
-      // (rows past Sq are clipped by the tensor map).
+      // the rows go out through this warp's staging slab: one TMA store
+      // (rows past Sq are clipped by the tensor map) and, for a fused
+      // all-gather, bulk copies of the valid rows to the further destinations.
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(bar_o_done, (uint32_t)(ns - 1) & 1, p.status));
       if (!ok) break;
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 13 : 5, k);
@@ -579,8 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive(bar_o_free);
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 14 : 6, k);
       const float inv = 1.f / l;
-      // the previous item's store must have finished reading the slab
-      if (lane == 0) ptx::bulk_wait_group_read0();
+      // the previous item's copies must have finished reading the slab
+      ptx::bulk_wait_group_read0();
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -590,40 +593,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         w.y = ptx::pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
         w.z = ptx::pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
         w.w = ptx::pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-        *reinterpret_cast<uint4 *>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = w;
+        *reinterpret_cast<uint4 *>(stage + lane * 128 + (c << 4)) = w;
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        ptx::tma_store_4d(&tm_o, ptx::smem_u32(stage), 0, (int)(q_tile + 32 * (warp & 3)), it.h,
-                          it.b);
-        ptx::bulk_commit_group();
-      }
+      const int64_t row0 = q_tile + 32 * (warp & 3);
+      if (lane == 0)
+        ptx::tma_store_4d(&tm_o, ptx::smem_u32(stage), 0, (int)row0, it.h, it.b);
       if (p.n_remote > 0) {
         // The further destinations (the all-gather of a head-sharded prefill:
-        // other GPUs' buffers, written over NVLink): 16-byte stores read back
-        // from the slab, eight lanes per 128-byte row so every row goes out as
-        // whole lines; rows past Sq are skipped.
-        const int64_t row0 = q_tile + 32 * (warp & 3);
+        // other GPUs' buffers, written over NVLink) get the slab's valid rows
+        // (those below Sq) by untiled bulk copies: one copy per destination
+        // when the rows are contiguous there, else one per row, each lane
+        // copying its own row.
+        const int nrows = (int)imin64(32, p.Sq - row0);
         const int64_t head = it.b * p.os_b + it.h * p.os_h;
-        const int ch = lane & 7;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = 4 * i + (lane >> 3);
-          const uint4 w =
-              *reinterpret_cast<const uint4 *>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
-          if (row0 + r < p.Sq) {
-            const int64_t off = 2 * (head + (row0 + r) * p.os_s) + 16 * ch;
+        if (p.os_s == kD) {
+          if (lane == 0 && nrows > 0) {
+            const int64_t off = 2 * (head + row0 * kD);
 #pragma unroll
             for (int d = 0; d < kMaxOutputPeers - 1; ++d)
-              if (d < p.n_remote) *reinterpret_cast<uint4 *>(p.remote[d] + off) = w;
+              if (d < p.n_remote)
+                ptx::bulk_store(p.remote[d] + off, ptx::smem_u32(stage), (uint32_t)nrows * 128);
           }
+        } else if (lane < nrows) {
+          const int64_t off = 2 * (head + (row0 + lane) * p.os_s);
+#pragma unroll
+          for (int d = 0; d < kMaxOutputPeers - 1; ++d)
+            if (d < p.n_remote)
+              ptx::bulk_store(p.remote[d] + off, ptx::smem_u32(stage + lane * 128), 128);
         }
       }
+      ptx::bulk_commit_group();
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 15 : 9, k);
     }
-    // Outstanding output stores must complete before the CTA exits.
-    if (lane == 0) ptx::bulk_wait_group0();
+    // Outstanding output copies must complete before the CTA exits.
+    ptx::bulk_wait_group0();
     if (!ok) set_abort(sm);
     if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, ok ? 5 : 6);
   }
@@ -660,11 +665,12 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
       !make_bf16_map_64x128(&tk, a.k, a.B, a.H, a.Sk, a.ks) ||
       !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
     return cudaErrorInvalidValue;
-  // The first destination (on this GPU) takes TMA stores of 32-row slabs; the
-  // others, plain stores.
+  // The first destination (on this GPU) takes TMA tensor stores of 32-row
+  // row-major slabs; the others, untiled bulk copies of the same slabs.
   CUtensorMap to;
   if (a.n_peers > kMaxOutputPeers ||
-      !make_bf16_map_64xR(&to, a.n_peers > 0 ? a.o_peers[0] : a.o, a.B, a.H, a.Sq, a.os, 32))
+      !make_bf16_map(&to, a.n_peers > 0 ? a.o_peers[0] : a.o, a.B, a.H, a.Sq, a.os, 64, 32,
+                     false))
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
     return cudaErrorInvalidValue;

@@ -1,5 +1,8 @@
 // decode_sm100.cu -- decode attention (one query token per (batch, head))
-// over a padded bf16 KV cache, split over 256-key chunks (split-KV).
+// over a padded KV cache, split over key chunks (split-KV): bf16 caches in
+// 256-key chunks, f32 caches (the reference-accurate path, e.g. GPT-2 in f32
+// with a KV cache) in 128-key chunks -- 32 KB of K and 32 KB of V per chunk
+// either way.
 //
 // The step is HBM-bound: every valid K and V byte is read exactly once and
 // nothing else of size is touched.  A persistent grid (one CTA per SM) walks
@@ -32,29 +35,59 @@
 namespace wfattn {
 namespace {
 
-constexpr int kChunk = 256;  // keys per work item
 constexpr int kD = 64;
 constexpr int kStages = 3;
 constexpr int kConsumerWarps = 16;
-constexpr int kKeysPerWarp = kChunk / kConsumerWarps;
-constexpr int kSteps = kKeysPerWarp / 4;  // 4 keys per warp step (8 lanes each)
 constexpr int kProducerWarp = kConsumerWarps, kMergeWarp = kConsumerWarps + 1;
 constexpr int kThreads = 32 * (kConsumerWarps + 2);
-constexpr uint32_t kRowBytes = kD * 2;
-constexpr uint32_t kStageBytes = kChunk * kRowBytes;
+constexpr uint32_t kStageBytes = 32 * 1024;  // K (and V) rows of one chunk
 constexpr int kPartFloats = kD + 2;  // acc[64], m, l
 constexpr int kMergeStride = kD + 4;  // a warp's row in smem: acc[64], m, l, pad to 16 B
 constexpr int kPlanMaxB = 1024;  // batches the in-smem work plan can order
+
+// Per element type of q and the cache: row size, chunk length, and the load of
+// the 8 consecutive elements a lane works on, widened to f32.
+template <typename T>
+struct Elem;
+template <>
+struct Elem<uint16_t> {  // bf16
+  static constexpr uint32_t kRowBytes = kD * 2;
+  __device__ static __forceinline__ void load8(const uint8_t *p, float (&f)[8]) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(p);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(u[i] << 16);
+      f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+  }
+};
+template <>
+struct Elem<float> {
+  static constexpr uint32_t kRowBytes = kD * 4;
+  __device__ static __forceinline__ void load8(const uint8_t *p, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(p);
+    const float4 b = *reinterpret_cast<const float4 *>(p + 16);
+    f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w;
+    f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
+  }
+};
+// keys per work item: 256 (bf16), 128 (f32)
+template <typename T>
+struct Chunk {
+  static constexpr int value = (int)(kStageBytes / Elem<T>::kRowBytes);
+};
 
 struct ItemInfo {
   int64_t bh;
   int c, n;  // chunk index, valid keys (-1: no more work)
 };
 
+template <typename T>
 struct DecSmem {
   uint8_t k[kStages][kStageBytes];
   uint8_t v[kStages][kStageBytes];
-  uint8_t q[kStages][kRowBytes];
+  uint8_t q[kStages][Elem<T>::kRowBytes];
   float merge[kStages][kConsumerWarps][kMergeStride];  // warp partials of a use of a stage
   ItemInfo item[kStages];        // written by the producer, read by the consumers
   ItemInfo merge_item[kStages];  // copy for the merge warp (item[] is refilled earlier)
@@ -69,7 +102,7 @@ struct DecSmem {
 
 struct DecParams {
   int64_t B, H, max_len;
-  int nch;  // chunks per (batch, head) = ceil(max_len / kChunk)
+  int nch;  // chunks per (batch, head) = ceil(max_len / chunk)
   const char *q, *k, *v;
   int64_t qs_b, qs_h, ks_b, ks_h, vs_b, vs_h;  // element strides (seq stride is kD)
   const int32_t *kv_lens;
@@ -86,18 +119,14 @@ __device__ __forceinline__ int64_t clamp_len(int32_t L, int64_t max_len, unsigne
   return L;
 }
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4 &w, float (&f)[8]) {
-  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(u[i] << 16);
-    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
-  }
-}
-
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecParams p) {
+  constexpr int kChunk = Chunk<T>::value;
+  constexpr uint32_t kRowBytes = Elem<T>::kRowBytes;
+  constexpr int kKeysPerWarp = kChunk / kConsumerWarps;
+  constexpr int kSteps = kKeysPerWarp / 4;  // 4 keys per warp step (8 lanes each)
   extern __shared__ __align__(128) uint8_t dsm_raw[];
-  DecSmem &sm = *reinterpret_cast<DecSmem *>(dsm_raw);
+  DecSmem<T> &sm = *reinterpret_cast<DecSmem<T> *>(dsm_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (ptx::timeout_flagged(p.status)) return;  // sticky until the host clears it
   volatile uint32_t &abort_flag = sm.abort;
@@ -212,9 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecPara
         sm.item[st].c = c;
         sm.item[st].n = n;
         const uint32_t bytes = (uint32_t)n * kRowBytes;
-        const char *qsrc = p.q + 2 * (b * p.qs_b + h * p.qs_h);
-        const char *ksrc = p.k + 2 * (b * p.ks_b + h * p.ks_h + t0 * kD);
-        const char *vsrc = p.v + 2 * (b * p.vs_b + h * p.vs_h + t0 * kD);
+        constexpr int64_t es = sizeof(T);
+        const char *qsrc = p.q + es * (b * p.qs_b + h * p.qs_h);
+        const char *ksrc = p.k + es * (b * p.ks_b + h * p.ks_h + t0 * kD);
+        const char *vsrc = p.v + es * (b * p.vs_b + h * p.vs_h + t0 * kD);
         const uint32_t fb = ptx::smem_u32(&sm.full[st]);
         ptx::mbar_arrive_expect_tx(fb, 2 * bytes + kRowBytes);
         ptx::bulk_load(ptx::smem_u32(sm.q[st]), qsrc, kRowBytes, fb);
@@ -311,15 +341,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecPara
     const int n = item.n;
 
     // Query slice of this lane: columns [8g, 8g+8), pre-scaled.
+    constexpr uint32_t kLaneBytes = 8 * sizeof(T);
     float qf[8];
-    bf16x8_to_f32(*reinterpret_cast<const uint4 *>(sm.q[st] + g * 16), qf);
+    Elem<T>::load8(sm.q[st] + g * kLaneBytes, qf);
 #pragma unroll
     for (int i = 0; i < 8; ++i) qf[i] *= p.scale_log2;
 
     // ---- scores of this warp's keys t_i = kKeysPerWarp*warp + 4*i + sub (all
     // 8 lanes of a key group end up holding its score).
     const int t_base = kKeysPerWarp * warp + sub;
-    const uint8_t *ks = sm.k[st] + g * 16;
+    const uint8_t *ks = sm.k[st] + g * kLaneBytes;
     float sc[kSteps];
 #pragma unroll
     for (int i = 0; i < kSteps; ++i) {
@@ -327,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecPara
       float d = 0.f;
       if (t < n) {
         float kf[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(ks + t * kRowBytes), kf);
+        Elem<T>::load8(ks + t * kRowBytes, kf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) d = fmaf(qf[e], kf[e], d);
       }
@@ -355,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecPara
     l += __shfl_xor_sync(0xffffffffu, l, 8);
     l += __shfl_xor_sync(0xffffffffu, l, 16);
     // ---- P.V over the same keys; lane holds columns [8g, 8g+8)
-    const uint8_t *vs = sm.v[st] + g * 16;
+    const uint8_t *vs = sm.v[st] + g * kLaneBytes;
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -364,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const DecPara
       const int t = t_base + 4 * i;
       if (t < n) {
         float vf[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(vs + t * kRowBytes), vf);
+        Elem<T>::load8(vs + t * kRowBytes, vf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] = fmaf(sc[i], vf[e], acc[e]);
       }
@@ -402,6 +433,7 @@ struct CombineParams {
 };
 
 // One warp per (batch, head): merge the chunk partials, write f32 output.
+template <int kChunk>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t bh = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -468,15 +500,20 @@ bool decode_shape_ok(int64_t B, int64_t H, int64_t max_len) {
          !__builtin_mul_overflow(B, H, &bh) && bh <= INT32_MAX;
 }
 
-size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t) {
-  // Within decode_shape_ok's bounds: B*H < 2^31 and nch < 2^23, so the
-  // partial count stays below 2^54 and the byte count below 2^63.
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t, bool f32) {
+  // Within decode_shape_ok's bounds: B*H < 2^31 and nch < 2^24, so the
+  // partial count stays below 2^55 and the byte count below 2^63.
   if (!decode_shape_ok(B, H, max_len)) return 0;
-  const int64_t nch = (max_len + kChunk - 1) / kChunk;
+  const int64_t chunk = f32 ? Chunk<float>::value : Chunk<uint16_t>::value;
+  const int64_t nch = (max_len + chunk - 1) / chunk;
   return (size_t)(B * H * nch) * kPartFloats * sizeof(float);
 }
 
-cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
+namespace {
+
+template <typename T>
+cudaError_t launch_decode_t(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
+  constexpr int kChunk = Chunk<T>::value;
   if (a.ks.s != kD || a.vs.s != kD) return cudaErrorInvalidValue;  // rows must be contiguous
   if (!decode_shape_ok(a.B, a.H, a.max_len)) return cudaErrorInvalidValue;
   DecParams p;
@@ -499,12 +536,12 @@ cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaS
   p.status = dev.status;
   const int64_t items = a.B * a.H * p.nch;
   const int64_t blocks = items < dev.sm_count ? items : dev.sm_count;
-  static_assert(sizeof(DecSmem) <= 227 * 1024, "shared memory budget");
-  const size_t smem = sizeof(DecSmem);
-  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(decode_split_kernel),
+  static_assert(sizeof(DecSmem<T>) <= 227 * 1024, "shared memory budget");
+  const size_t smem = sizeof(DecSmem<T>);
+  cudaError_t err = ensure_smem_attr(reinterpret_cast<const void *>(decode_split_kernel<T>),
                                      (int)smem, dev.device);
   if (err != cudaSuccess) return err;
-  decode_split_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(p);
+  decode_split_kernel<T><<<(unsigned)blocks, kThreads, smem, stream>>>(p);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   CombineParams cp;
@@ -517,8 +554,14 @@ cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaS
   cp.o = a.o;
   cp.os_b = a.os.b;
   cp.os_h = a.os.h;
-  decode_combine_kernel<<<(unsigned)((cp.BH + 3) / 4), 128, 0, stream>>>(cp);
+  decode_combine_kernel<kChunk><<<(unsigned)((cp.BH + 3) / 4), 128, 0, stream>>>(cp);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream) {
+  return a.f32 ? launch_decode_t<float>(a, dev, stream) : launch_decode_t<uint16_t>(a, dev, stream);
 }
 
 }  // namespace wfattn

@@ -261,9 +261,9 @@ wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_
   a.n_peers = n_outputs;
   st = check_bf16(a);
   if (st != WFATTN_OK) return st;
-  // q, k, v (TMA loads) and outputs[0] (TMA stores) must be this GPU's own
-  // memory: the kernel reaches other GPUs' buffers only through the plain
-  // stores to outputs[1..].
+  // q, k, v (TMA loads) and outputs[0] (TMA tensor stores) must be this GPU's
+  // own memory: the kernel reaches other GPUs' buffers only through the
+  // untiled bulk copies to outputs[1..].
   const void *local[4] = {q, k, v, outputs[0]};
   const char *names[4] = {"q", "k", "v", "outputs[0]"};
   for (int i = 0; i < 4; ++i) {
@@ -305,16 +305,26 @@ wfattn_status_t wfattn_attention(const float *Q, const float *K, const float *V,
 size_t wfattn_decode_workspace_size(int64_t batch, int64_t heads, int64_t max_kv_len,
                                     int64_t head_dim) {
   if (head_dim < 1) return 0;
-  return decode_workspace_bytes(batch, heads, max_kv_len, head_dim);  // 0 for a bad shape
+  return decode_workspace_bytes(batch, heads, max_kv_len, head_dim, false);  // 0: bad shape
 }
 
-wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, int64_t max_kv_len,
-                              const void *q, const int64_t *q_strides, const void *k_cache,
-                              const int64_t *k_strides, const void *v_cache,
+size_t wfattn_decode_f32_workspace_size(int64_t batch, int64_t heads, int64_t max_kv_len,
+                                        int64_t head_dim) {
+  if (head_dim < 1) return 0;
+  return decode_workspace_bytes(batch, heads, max_kv_len, head_dim, true);  // 0: bad shape
+}
+
+}  // extern "C"
+
+namespace {
+
+// Argument checks and launch shared by the bf16 and f32 decode entry points.
+wfattn_status_t decode_common(bool f32, int64_t batch, int64_t heads, int64_t head_dim,
+                              int64_t max_kv_len, const void *q, const int64_t *q_strides,
+                              const void *k_cache, const int64_t *k_strides, const void *v_cache,
                               const int64_t *v_strides, const int32_t *kv_lens, float *o,
                               const int64_t *o_strides, float scale, void *workspace,
                               size_t workspace_bytes, void *stream) {
-  t_last_error.clear();
   if (!q || !k_cache || !v_cache || !kv_lens || !o)
     return fail(WFATTN_INVALID_ARG, "null tensor pointer");
   if (batch < 1 || heads < 1 || max_kv_len < 1 || head_dim < 1)
@@ -324,7 +334,7 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
                 "decode needs batch*heads <= 2^31-1 and max_kv_len <= 2^31-1 (B=%lld H=%lld "
                 "max_kv_len=%lld)", (long long)batch, (long long)heads, (long long)max_kv_len);
   if (head_dim != 64) return fail(WFATTN_UNSUPPORTED, "decode supports head_dim == 64 only");
-  const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
+  const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim, f32);
   if (!workspace || workspace_bytes < need)
     return fail(WFATTN_INVALID_ARG, "workspace of %zu bytes needed, %zu given", need,
                 workspace ? workspace_bytes : (size_t)0);
@@ -332,6 +342,7 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
   if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(o) || !al16(workspace))
     return fail(WFATTN_INVALID_ARG, "decode tensors and workspace must be 16-byte aligned");
   DecodeArgs a;
+  a.f32 = f32;
   a.B = batch;
   a.H = heads;
   a.D = head_dim;
@@ -350,9 +361,12 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
   a.workspace_bytes = workspace_bytes;
   if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os))
     return fail(WFATTN_INVALID_ARG, "negative stride");
-  if (a.qs.b % 8 || a.qs.h % 8 || a.ks.b % 8 || a.ks.h % 8 || a.ks.s % 8 || a.vs.b % 8 ||
-      a.vs.h % 8 || a.vs.s % 8)
-    return fail(WFATTN_INVALID_ARG, "bf16 q/k/v strides must be multiples of 8 elements");
+  // 16-byte aligned rows for the bulk copies: 8 bf16 or 4 f32 elements
+  const int64_t m = f32 ? 4 : 8;
+  if (a.qs.b % m || a.qs.h % m || a.ks.b % m || a.ks.h % m || a.ks.s % m || a.vs.b % m ||
+      a.vs.h % m || a.vs.s % m)
+    return fail(WFATTN_INVALID_ARG, "%s q/k/v strides must be multiples of %d elements",
+                f32 ? "f32" : "bf16", (int)m);
   if (a.ks.s != head_dim || a.vs.s != head_dim)
     return fail(WFATTN_UNSUPPORTED, "decode needs contiguous cache rows (seq stride == head_dim)");
   if (a.os.b % 4 || a.os.h % 4)
@@ -363,9 +377,38 @@ wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, in
   if (!is_sm100(dev))
     return fail(WFATTN_UNSUPPORTED, "libwfattn is built for sm_100a; device %d is sm_%d%d",
                 dev.device, dev.cc_major, dev.cc_minor);
-  cudaError_t err = launch_decode_bf16(a, dev, static_cast<cudaStream_t>(stream));
+  cudaError_t err = launch_decode(a, dev, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "decode launch");
   return WFATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+wfattn_status_t wfattn_decode(int64_t batch, int64_t heads, int64_t head_dim, int64_t max_kv_len,
+                              const void *q, const int64_t *q_strides, const void *k_cache,
+                              const int64_t *k_strides, const void *v_cache,
+                              const int64_t *v_strides, const int32_t *kv_lens, float *o,
+                              const int64_t *o_strides, float scale, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  t_last_error.clear();
+  return decode_common(false, batch, heads, head_dim, max_kv_len, q, q_strides, k_cache,
+                       k_strides, v_cache, v_strides, kv_lens, o, o_strides, scale, workspace,
+                       workspace_bytes, stream);
+}
+
+wfattn_status_t wfattn_decode_f32(int64_t batch, int64_t heads, int64_t head_dim,
+                                  int64_t max_kv_len, const float *q, const int64_t *q_strides,
+                                  const float *k_cache, const int64_t *k_strides,
+                                  const float *v_cache, const int64_t *v_strides,
+                                  const int32_t *kv_lens, float *o, const int64_t *o_strides,
+                                  float scale, void *workspace, size_t workspace_bytes,
+                                  void *stream) {
+  t_last_error.clear();
+  return decode_common(true, batch, heads, head_dim, max_kv_len, q, q_strides, k_cache,
+                       k_strides, v_cache, v_strides, kv_lens, o, o_strides, scale, workspace,
+                       workspace_bytes, stream);
 }
 
 // Decode for callers that cannot allocate device memory: the split-KV
@@ -386,7 +429,7 @@ wfattn_status_t wfattn_decode_noalloc(int64_t batch, int64_t heads, int64_t head
     return fail(WFATTN_INVALID_ARG,
                 "decode needs batch*heads <= 2^31-1 and max_kv_len <= 2^31-1 (B=%lld H=%lld "
                 "max_kv_len=%lld)", (long long)batch, (long long)heads, (long long)max_kv_len);
-  const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim);
+  const size_t need = decode_workspace_bytes(batch, heads, max_kv_len, head_dim, false);
   if (need > kDecodeNoAllocScratchBytes)
     return fail(WFATTN_INVALID_ARG,
                 "wfattn_decode_noalloc: this shape needs %zu bytes of scratch but the static "

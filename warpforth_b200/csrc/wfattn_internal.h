@@ -38,8 +38,9 @@ struct PrefillArgs {
 };
 
 struct DecodeArgs {
+  bool f32 = false;  // q, k, v are f32 (else bf16)
   int64_t B, H, D, max_len;
-  const void *q;  // bf16 [B, H, D]
+  const void *q;  // [B, H, D]
   Strides3 qs;    // s unused
   const void *k, *v;
   Strides3 ks, vs;
@@ -75,9 +76,10 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
 // Decode shapes the kernels index safely: sizes >= 1, max_len <= 2^31 - 1,
 // B*H <= 2^31 - 1 (checked without overflow).
 bool decode_shape_ok(int64_t B, int64_t H, int64_t max_len);
-// Workspace bytes of a decode call (0 when decode_shape_ok fails).
-size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t D);
-cudaError_t launch_decode_bf16(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream);
+// Workspace bytes of a decode call over a bf16 (f32 = false) or f32 cache
+// (0 when decode_shape_ok fails).
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t max_len, int64_t D, bool f32);
+cudaError_t launch_decode(const DecodeArgs &a, const DeviceInfo &dev, cudaStream_t stream);
 
 // Size of the static device scratch behind wfattn_decode_noalloc (8 MiB).
 constexpr size_t kDecodeNoAllocScratchBytes = size_t(8) << 20;

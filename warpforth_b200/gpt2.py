@@ -10,9 +10,10 @@ q/k/v views without copies, and runs on torch's current stream.
 Semantics kept from the reference: causal masking only -- ``attention_mask``
 (padding) and ``dropout`` are ignored, exactly as the reference ignores them;
 ``scaling`` is honoured (GPT-2 passes 1/sqrt(head_dim), the reference kernel's
-fixed scale).  With a KV cache (``use_cache=True``) the single new query is
-aligned with the end of the keys, so cached generation works too; the
-reference only supports ``use_cache=False``.
+fixed scale).  With a KV cache (``use_cache=True``, which the reference does
+not support) the prompt goes through the prefill kernel and every later
+single-token step through the split-KV decode kernel (``wfattn_decode_f32``
+for the f32 model) over the cached keys and values.
 
     python -m warpforth_b200.gpt2 --max-tokens 128      # random-init GPT-2 small
 """
@@ -25,18 +26,46 @@ from collections.abc import Callable
 
 import torch
 
-from .warpforth import attention
+from .warpforth import DecodeWorkspace, attention, decode
+
+
+# library calls made by the patched attention, by kind (read by count_calls)
+_calls = {"prefill": 0, "decode": 0}
 
 
 def make_warpforth_eager_attn() -> Callable:
     """Replacement for transformers' eager_attention_forward (see the module docstring)."""
 
+    workspace = DecodeWorkspace()
+    lens_cache: dict = {}
+
     def warpforth_eager_attn(module, query, key, value, attention_mask=None, scaling=None,
                              dropout=0.0, **kwargs):
+        b, _, sq, d = query.shape
+        sk = key.shape[2]
+        if (sq == 1 and sk > 1 and query.dtype in (torch.float32, torch.bfloat16)
+                and d == 64 and key.stride(2) == d and value.stride(2) == d
+                and key.stride(3) == 1 and value.stride(3) == 1):
+            # one new token against the cached keys: the decode kernel
+            _calls["decode"] += 1
+            lens = lens_cache.get((b, sk, query.device))
+            if lens is None:
+                lens = torch.full((b,), sk, dtype=torch.int32, device=query.device)
+                lens_cache[(b, sk, query.device)] = lens
+            out = decode(query, key, value, lens, scale=scaling, workspace=workspace)
+            return out.to(query.dtype).unsqueeze(1), None
+        _calls["prefill"] += 1
         out = attention(query, key, value, causal=True, scale=scaling)
         return out.transpose(1, 2), None
 
     return warpforth_eager_attn
+
+
+def count_calls(fn: Callable[[], object]) -> dict:
+    """Runs fn() and returns how many prefill and decode calls the patched attention made."""
+    before = dict(_calls)
+    fn()
+    return {k: _calls[k] - before[k] for k in _calls}
 
 
 def patch_gpt2() -> Callable[[], None]:

@@ -146,8 +146,8 @@ class ShardedPrefill:
         self.slots = (buf[0], buf[1])
         esz = buf.element_size()
         # this rank's heads inside every rank's output slot, as mapped on this GPU; its
-        # own buffer first (the kernel's TMA stores go to the first destination only,
-        # the other GPUs' buffers get plain stores)
+        # own buffer first (the kernel's TMA tensor stores go to the first destination
+        # only, the other GPUs' buffers get bulk copies of the same output slabs)
         head_off = self.rank * self.local_heads * buf.stride(2) * esz
         slot_bytes = buf.stride(0) * esz
         order = [self.rank] + [r for r in range(self.world) if r != self.rank]

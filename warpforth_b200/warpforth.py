@@ -140,9 +140,10 @@ def attention_gather_ptrs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     """``attention_gather`` with raw output addresses: each ``out_ptrs[i]`` is the start of
     a [B, H, Sq, 64] bf16 view with element strides ``out_strides`` = (batch, head, seq),
     e.g. this rank's heads inside every rank's ``peer.PeerBuffer`` as mapped on this GPU.
-    ``out_ptrs[0]`` must be this GPU's own memory (it takes TMA stores; the others get
-    plain stores).  The stores into other GPUs' buffers are complete when the kernel is;
-    the caller synchronises with those GPUs afterwards."""
+    ``out_ptrs[0]`` must be this GPU's own memory, as must q, k and v (TMA tensor loads
+    and stores); the others get bulk copies of each finished output slab.  The copies
+    into other GPUs' buffers are complete when the kernel is; the caller synchronises
+    with those GPUs afterwards."""
     _check_bf16_qkv(q, k, v)
     if not 1 <= len(out_ptrs) <= 8:
         raise ValueError("out_ptrs must hold 1 to 8 addresses")
@@ -168,26 +169,31 @@ class DecodeWorkspace:
         return self.buffer
 
 
-def decode_workspace_size(batch: int, heads: int, max_kv_len: int, head_dim: int) -> int:
-    return int(_lib.load().wfattn_decode_workspace_size(batch, heads, max_kv_len, head_dim))
+def decode_workspace_size(batch: int, heads: int, max_kv_len: int, head_dim: int,
+                          dtype: torch.dtype = torch.bfloat16) -> int:
+    lib = _lib.load()
+    fn = lib.wfattn_decode_f32_workspace_size if dtype == torch.float32 else \
+        lib.wfattn_decode_workspace_size
+    return int(fn(batch, heads, max_kv_len, head_dim))
 
 
 def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_lens: torch.Tensor,
            *, scale: float | None = None, out: torch.Tensor | None = None,
            workspace: DecodeWorkspace | None = None) -> torch.Tensor:
-    """One-token decode attention over a padded bf16 KV cache (split-KV).
+    """One-token decode attention over a padded KV cache (split-KV).
 
-    q: bf16 [B, H, D] or [B, H, 1, D]; k_cache / v_cache: bf16 [B, H, Lmax, D]
-    with contiguous rows; kv_lens: int32 CUDA [B] with 1 <= kv_lens[b] <= Lmax.
-    Returns f32 [B, H, D].
+    q: [B, H, D] or [B, H, 1, D]; k_cache / v_cache: [B, H, Lmax, D] with
+    contiguous rows; all three bf16 (``wfattn_decode``) or all f32
+    (``wfattn_decode_f32``, the reference-accurate path); kv_lens: int32 CUDA
+    [B] with 1 <= kv_lens[b] <= Lmax.  Returns f32 [B, H, D].
     """
     if q.dim() == 4:
         q = q[:, :, 0, :]
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("kv_lens", kv_lens)):
         _require_cuda(name, t)
-    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or \
-            v_cache.dtype != torch.bfloat16:
-        raise ValueError("decode expects bfloat16 q / k_cache / v_cache")
+    if q.dtype not in (torch.bfloat16, torch.float32) or k_cache.dtype != q.dtype or \
+            v_cache.dtype != q.dtype:
+        raise ValueError("decode expects q / k_cache / v_cache all bfloat16 or all float32")
     if kv_lens.dtype != torch.int32:
         raise ValueError("kv_lens must be int32")
     b, h, d = q.shape
@@ -196,13 +202,15 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len
         raise ValueError("cache shape mismatch")
     if out is None:
         out = torch.empty((b, h, d), dtype=torch.float32, device=q.device)
-    ws = (workspace or DecodeWorkspace()).get(decode_workspace_size(b, h, lmax, d), q.device)
+    ws = (workspace or DecodeWorkspace()).get(decode_workspace_size(b, h, lmax, d, q.dtype),
+                                              q.device)
     lib = _lib.load()
     qs = _lib.strides_arg(q.stride()[:2])
     ks = _lib.strides_arg(k_cache.stride()[:3])
     vs = _lib.strides_arg(v_cache.stride()[:3])
     os_ = _lib.strides_arg(out.stride()[:2])
-    _lib.check(lib.wfattn_decode(
+    fn = lib.wfattn_decode_f32 if q.dtype == torch.float32 else lib.wfattn_decode
+    _lib.check(fn(
         b, h, d, lmax, _ptr(q), qs, _ptr(k_cache), ks, _ptr(v_cache), vs, _ptr(kv_lens),
         _ptr(out), os_, float(scale) if scale else 0.0, _ptr(ws), ws.numel(),
         _stream_handle(q.device)))

@@ -628,30 +628,59 @@ def run_prefill(args, ctx: Ctx, w: Workload) -> dict:
     shape = (w.B, heads, w.S, w.D)
     host = [torch.randn(*shape, generator=g).to(tdt).pin_memory() for _ in range(3)]
     dev_in = [torch.empty(shape, dtype=tdt, device=dev) for _ in range(3)]
-    if sp is not None:
+    # One GPU holds every head: the step goes through wf.attention in batch chunks, so the
+    # copies in (one stream) and out (another stream) overlap other chunks' compute.
+    # Several GPUs: this rank's heads go in, the gathered output comes out on rank 0.
+    pipelined = w.B >= 4 and (sp is None or ctx.world == 1)
+    if sp is not None and not pipelined:
         host_out = torch.empty((w.B, w.H, w.S, w.D), dtype=tdt).pin_memory() \
             if ctx.rank == 0 else None
     else:
         res = torch.empty(shape, dtype=tdt, device=dev)
         host_out = torch.empty(shape, dtype=tdt).pin_memory()
+    cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    nchunk = 4
+    bounds = [(c * w.B // nchunk, (c + 1) * w.B // nchunk) for c in range(nchunk)]
 
     def one():
+        if pipelined:
+            main = torch.cuda.current_stream(dev)
+            cs_in.wait_stream(main)
+            cs_out.wait_stream(main)
+            arrived = []
+            with torch.cuda.stream(cs_in):
+                for b0, b1 in bounds:
+                    for h_, d_ in zip(host, dev_in):
+                        d_[b0:b1].copy_(h_[b0:b1], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(cs_in)
+                    arrived.append(e)
+            for (b0, b1), e in zip(bounds, arrived):
+                main.wait_event(e)
+                wf.attention(*(t[b0:b1] for t in dev_in), out=res[b0:b1])
+                done = torch.cuda.Event()
+                done.record(main)
+                cs_out.wait_event(done)
+                with torch.cuda.stream(cs_out):
+                    host_out[b0:b1].copy_(res[b0:b1], non_blocking=True)
+            main.wait_stream(cs_out)
+            return
         for h_, d_ in zip(host, dev_in):
             d_.copy_(h_, non_blocking=True)
-        if sp is not None:
-            out_ = sp(*(sp.split_local(t) for t in dev_in))
-            if host_out is not None:
-                host_out.copy_(out_, non_blocking=True)
-        else:
-            wf.attention(*dev_in, out=res)
-            host_out.copy_(res, non_blocking=True)
+        out_ = sp(*(sp.split_local(t) for t in dev_in))
+        if host_out is not None:
+            host_out.copy_(out_, non_blocking=True)
 
     e2e_ms = timed_e2e(ctx, one, steps, args.warmup, flush)
     e2e = {"value": units / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
            "steps": steps, "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
            "d2h_bytes_per_step": host_out.numel() * host_out.element_size() if host_out is not None
            else 0,
-           "path": "warpforth_b200.warpforth (ctypes) -> libwfattn C ABI, pinned host buffers"}
+           "path": ("warpforth_b200.warpforth.attention (ctypes) -> libwfattn C ABI, pinned host "
+                    f"buffers; the batch in {nchunk} chunks, copies in and out on two side "
+                    "streams overlapping the other chunks' compute") if pipelined else
+                   "ShardedPrefill -> libwfattn C ABI, this rank's q/k/v in from pinned host "
+                   "buffers, the gathered output out on rank 0"}
     del host, dev_in
 
     if w.dtype == "f32":

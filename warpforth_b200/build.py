@@ -6,6 +6,7 @@
 Outputs (git-ignored, shipped with the source tree):
     warpforth_b200/lib/libwfattn.so
     warpforth_b200/lib/wfattn-runner
+    warpforth_b200/lib/wfattn-mma-probe  (tensor-core issue-rate probe behind the kernel design)
 """
 
 from __future__ import annotations
@@ -25,6 +26,8 @@ LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libwfattn.so"
 RUNNER = LIB_DIR / "wfattn-runner"
 RUNNER_SRC = PKG / "runner" / "wfattn_runner.cpp"
+PROBE = LIB_DIR / "wfattn-mma-probe"
+PROBE_SRC = CSRC / "mma_rate_probe.cu"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -89,6 +92,9 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
               "-I", "/usr/local/cuda/include", str(RUNNER_SRC), "-o", str(RUNNER),
               "-L", str(LIB_DIR), "-lwfattn", "-Wl,-rpath,$ORIGIN",
               "-L", "/usr/local/cuda/lib64", "-lcudart", "-Wl,-rpath,/usr/local/cuda/lib64"])
+    if PROBE_SRC.exists() and (force or _stale(PROBE, [PROBE_SRC, CSRC / "sm100_ptx.cuh"])):
+        _run([cc, "-std=c++17", "-O3", "-lineinfo", *ARCH, "-I", str(CSRC), "-I",
+              str(ROOT / "include"), str(PROBE_SRC), "-o", str(PROBE)])
     return LIB
 
 

@@ -96,10 +96,6 @@ struct Params {
   int64_t n_pairs;  // 256-row query blocks per (batch, head)
   int64_t n_items;  // n_pairs * B * H
   uint32_t group;   // consecutive blocks of one (batch, head) in the item order
-  // item decoding: full groups of `group` blocks cover the first full_items
-  // items; divisors group * B * H, group, the last group's size, H
-  uint32_t full_items, n_full;
-  FastDiv f_gbh, f_gs, f_gl, f_h;
   // Further destinations of the output (e.g. other GPUs' buffers mapped into
   // this one), written by untiled bulk copies; strides os_* are shared.
   char *remote[kMaxOutputPeers - 1];
@@ -129,23 +125,21 @@ __device__ __forceinline__ bool item_of(const Params &p, int k, Item &it) {
   const uint32_t G = gridDim.x;
   const uint32_t idx = (uint32_t)k * G + ((k & 1) ? G - 1 - blockIdx.x : blockIdx.x);
   if ((int64_t)idx >= p.n_items) return false;
-  // Divisions by launch constants go through fast_div (multiply-high and
-  // shift): the item decode sits on every role's path between two items.
-  const uint32_t gs = p.f_gs.d;
+  const uint32_t BH = (uint32_t)(p.B * p.H), H = (uint32_t)p.H;
+  const uint32_t NP = (uint32_t)p.n_pairs, gs = p.group, n_full = NP / gs;
   uint32_t blk, bh;
-  if (idx < p.full_items) {
-    const uint32_t g = fast_div(idx, p.f_gbh), r = idx - g * p.f_gbh.d;
-    bh = fast_div(r, p.f_gs);
+  if (idx < n_full * gs * BH) {
+    const uint32_t g = idx / (gs * BH), r = idx - g * (gs * BH);
+    bh = r / gs;
     blk = g * gs + (r - bh * gs);
   } else {  // the last, partial group
-    const uint32_t r = idx - p.full_items;
-    bh = fast_div(r, p.f_gl);
-    blk = p.n_full * gs + (r - bh * p.f_gl.d);
+    const uint32_t gl = NP - n_full * gs, r = idx - n_full * gs * BH;
+    bh = r / gl;
+    blk = n_full * gs + (r - bh * gl);
   }
   const int64_t qp = p.n_pairs - 1 - blk;
-  const uint32_t b = fast_div(bh, p.f_h);
-  it.b = (int)b;
-  it.h = (int)(bh - b * p.f_h.d);
+  it.b = (int)(bh / H);
+  it.h = (int)(bh - (uint32_t)it.b * H);
   it.q0 = qp * 2 * kBM;
   const int64_t off = p.Sk - p.Sq;
 #pragma unroll
@@ -587,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar_o_free);
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 14 : 6, k);
-      const float inv = ptx::rcp_approx(l);  // ~1 ulp; the output is rounded to bf16
+      const float inv = 1.f / l;
       // the previous item's copies must have finished reading the slab
       ptx::bulk_wait_group_read0();
       __syncwarp();
@@ -706,14 +700,6 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   // (long sequences, 16+ blocks per head); with few items per CTA the plain
   // heaviest-first order balances the CTAs better.
   p.group = (p.n_pairs >= 16 && p.n_items >= 32 * blocks) ? 8 : 1;
-  const uint32_t bh = (uint32_t)(a.B * a.H), np = (uint32_t)p.n_pairs;
-  p.n_full = np / p.group;
-  p.full_items = p.n_full * p.group * bh;  // <= n_items < 2^31
-  const uint32_t last = np - p.n_full * p.group;
-  p.f_gbh = make_fastdiv(p.group * bh);
-  p.f_gs = make_fastdiv(p.group);
-  p.f_gl = make_fastdiv(last > 0 ? last : 1);
-  p.f_h = make_fastdiv((uint32_t)a.H);
   prefill_bf16_2q_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }

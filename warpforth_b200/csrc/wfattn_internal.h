@@ -17,26 +17,6 @@ enum DeviceStatusBits : unsigned int {
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
 
-// Division of a 32-bit n by a divisor d (1 <= d < 2^31) fixed at launch, as a
-// multiply-high, an add and a shift (the round-up method of Granlund and
-// Montgomery, "Division by invariant integers using multiplication", 1994):
-// with s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1 (< 2^32),
-// n / d = (umulhi(n, m) + n) >> s for every 32-bit n.
-struct FastDiv {
-  uint32_t d, m, s;
-};
-inline FastDiv make_fastdiv(uint32_t d) {
-  uint32_t s = 0;
-  while ((uint64_t(1) << s) < d) ++s;
-  const uint64_t m = ((uint64_t(1) << 32) * ((uint64_t(1) << s) - d)) / d + 1;
-  return FastDiv{d, (uint32_t)m, s};
-}
-#ifdef __CUDACC__
-__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv &f) {
-  return (uint32_t)(((uint64_t)__umulhi(n, f.m) + n) >> f.s);
-}
-#endif
-
 // Strided [B, H, S, D] view (element strides, unit head_dim stride).
 struct Strides3 {
   int64_t b, h, s;

@@ -13,7 +13,7 @@ Workloads (all synthetic, seeded):
                           heads split evenly over the N ranks, O all-gathered.
                           One step = the whole batch.  Total work is fixed (strong scaling).
   prefill                 causal prefill [8, 12, 1024, 64] bf16, seed 2 (GPT-2 head shape).
-  prefill_f32             the same in f32 (the reference-accurate CUDA-core kernel).
+  prefill_f32             the same in f32 (the reference-accurate 3xTF32 tensor-core kernel).
   decode                  one-token decode, B=64, H=25, D=64, bf16 cache padded to 4096,
                           kv_lens ~ U[512, 4096] (seed 3); metric = valid KV bytes / s.
   gpt2                    GPT-2 small random init (seed 1), 32-token prompt, 128 greedy
@@ -123,6 +123,19 @@ def load_peaks() -> tuple[dict, str]:
 def f32_fma_peak(peaks: dict) -> float:
     """CUDA-core f32 FMA peak (TFLOP/s): 148 SMs x 128 lanes x 2 FLOP x max SM clock."""
     return 148 * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
+
+
+def f32_roof(ctx, D: int) -> dict:
+    """Roofline of the f32 prefill path.  head_dim 64 runs on the tensor cores: every product is
+    three tf32 MMAs (hi*hi + hi*lo + lo*hi) and tf32 issues at half the bf16 rate, so the ceiling
+    for the algorithmic FLOPs is the measured bf16 peak / 6.  Other head dims run on the CUDA
+    cores, bounded by the f32 FMA rate."""
+    if D == 64:
+        return {"bound": "tensor", "peak": float(ctx.peaks["bf16_tflops"]) / 6,
+                "peak_source": f"{ctx.peak_src} bf16_tflops / 2 (tf32 rate) / 3 (three tf32 "
+                "MMAs per product)", "kernel": "prefill_f32_tc_kernel"}
+    return {"bound": "fp32-simt", "peak": f32_fma_peak(ctx.peaks),
+            "peak_source": "nominal f32 FMA rate at max SM clock", "kernel": "prefill_f32_kernel"}
 
 
 # ------------------------------------------------------------------ clocks
@@ -684,9 +697,7 @@ def run_prefill(args, ctx: Ctx, w: Workload) -> dict:
     del host, dev_in
 
     if w.dtype == "f32":
-        peak = f32_fma_peak(ctx.peaks)
-        roof = {"bound": "fp32-simt", "peak": peak, "peak_source": "nominal f32 FMA rate at max "
-                "SM clock", "kernel": "prefill_f32_kernel"}
+        roof = f32_roof(ctx, w.D)
     else:
         key = "bf16_tflops_sustained" if (w.sharded and ms_per_step > 1000) else "bf16_tflops"
         roof = {"bound": "tensor", "peak": float(ctx.peaks[key]),
@@ -834,7 +845,7 @@ def run_head_call(args, ctx: Ctx, w: Workload) -> dict:
 
     e2e_ms = timed_e2e(ctx, one, 20, args.warmup, False)
     flops = prefill_flops(w)
-    peak = f32_fma_peak(ctx.peaks)
+    roof = f32_roof(ctx, w.D)
     achieved = flops / (us / 1e6) / 1e12
     line = {
         "metric": "GPT-2 attention call latency", "value": us, "unit": "us per call",
@@ -844,10 +855,9 @@ def run_head_call(args, ctx: Ctx, w: Workload) -> dict:
         "config": dict(config_of(w, 1), device_timing=f"CUDA events around {n_calls} graph "
                        "replays of the batched library call per step"),
         "roofline": {"bound": "latency (6.4 MFLOP per call: launch and fill dominate)",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "peak_source": "nominal f32 FMA rate at max SM "
-                     "clock", "kernel": "prefill_f32_kernel", "kernel_ms": us / 1e3,
-                     "traffic": None},
+                     "achieved": achieved, "peak": roof["peak"], "unit": "TFLOP/s",
+                     "frac": achieved / roof["peak"], "peak_source": roof["peak_source"],
+                     "kernel": roof["kernel"], "kernel_ms": us / 1e3, "traffic": None},
         "e2e": {"value": e2e_ms * 1e3, "unit": "us per call", "ms_per_step": e2e_ms, "steps": 20,
                 "h2d_bytes_per_step": 3 * host[0].numel() * 4,
                 "d2h_bytes_per_step": host_out.numel() * 4,
@@ -902,7 +912,8 @@ def run_gpt2(args, ctx: Ctx, w: Workload) -> dict:
     o = torch.empty_like(q)
     kms = _ref_time(ctx, graph_of(ctx, lambda: wf.attention(q, k, v, out=o)).replay, 100)
     kflops = 4 * 64 * 12 * (s_max * (s_max + 1) // 2)
-    peak = f32_fma_peak(ctx.peaks)
+    roof = f32_roof(ctx, 64)
+    peak = roof["peak"]
     line = {
         "metric": "GPT-2 gen tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -911,10 +922,10 @@ def run_gpt2(args, ctx: Ctx, w: Workload) -> dict:
         "config": dict(config_of(w, world), device_timing="CUDA events around whole "
                        "generate() calls (host launch path included)"),
         "roofline": {"bound": "launch/latency (attention is a small part of a GPT-2 step)",
-                     "kernel": f"prefill_f32_kernel at [1,12,{s_max},64]",
+                     "kernel": f"{roof['kernel']} at [1,12,{s_max},64]",
                      "achieved": kflops / (kms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": kflops / (kms / 1e3) / 1e12 / peak, "kernel_ms": kms,
-                     "traffic": None, "peak_source": "nominal f32 FMA rate at max SM clock",
+                     "traffic": None, "peak_source": roof["peak_source"],
                      "attention_calls_per_step": calls},
         "e2e": {"value": w.S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "steps": min(steps, args.e2e_steps),

@@ -35,8 +35,8 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "-I", str(ROOT / "include"),
 ]
-SOURCES = ["wfattn_api.cu", "attn_f32.cu", "attn_bf16_sm100.cu", "attn_bf16_2q_sm100.cu",
-           "decode_sm100.cu", "tma_map.cu"]
+SOURCES = ["wfattn_api.cu", "attn_f32.cu", "attn_f32_tc_sm100.cu", "attn_bf16_sm100.cu",
+           "attn_bf16_2q_sm100.cu", "decode_sm100.cu", "tma_map.cu"]
 HEADERS = ["wfattn_internal.h", "sm100_ptx.cuh", "tma_map.h", "exp2_poly.cuh"]
 
 

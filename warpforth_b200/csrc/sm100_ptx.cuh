@@ -274,6 +274,26 @@ __device__ __forceinline__ void mma_ts_lh(uint32_t d_tmem, uint32_t a_tmem, uint
       : "memory");
 }
 
+// kind::tf32 forms (f32 bit patterns in; the MMA uses their top 19 bits).
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 64 consecutive 32-bit TMEM columns of this thread's lane <-> registers (32x32b shape).
 __device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
@@ -347,6 +367,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, in
   return (1u << 4)                         // D format f32
          | (1u << 7)                       // A format bf16
          | (1u << 10)                      // B format bf16
+         | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17)        // N / 8
+         | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
+
+// Instruction descriptor for kind::tf32 with f32 accumulation (A, B format
+// code 2 = tf32).
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4)                         // D format f32
+         | (2u << 7)                       // A format tf32
+         | (2u << 10)                      // B format tf32
          | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
          ((uint32_t)(N >> 3) << 17)        // N / 8
          | ((uint32_t)(M >> 4) << 24);     // M / 16

@@ -49,6 +49,24 @@ bool make_bf16_map(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64
   return r == CUDA_SUCCESS;
 }
 
+bool make_f32_map(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
+                  const Strides3 &st, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {64, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st.s * 4, (cuuint64_t)st.h * 4, (cuuint64_t)st.b * 4};
+  const cuuint64_t extent[3] = {(cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  for (int i = 0; i < 3; ++i)
+    if (extent[i] == 1 && strides[i] == 0) strides[i] = 256;
+  const cuuint32_t box[4] = {32, (cuuint32_t)box_rows, 1, 1};  // 32 f32 = one 128-byte row
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_bf16_map_64xR(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
                         const Strides3 &st, int box_rows) {
   return make_bf16_map(m, base, B, H, S, st, 64, box_rows, true);

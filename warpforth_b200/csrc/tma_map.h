@@ -22,4 +22,10 @@ bool make_bf16_map_64xR(CUtensorMap *m, const void *base, int64_t B, int64_t H, 
 bool make_bf16_map(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
                    const Strides3 &st, int box_cols, int box_rows, bool swizzle128);
 
+// [B, H, S, 64] f32 view -> 4-D tensor map {64, S, H, B} with a box of
+// {32, box_rows, 1, 1} (one 128-byte row of 32 floats) and 128-byte swizzle;
+// a 64-column tile is loaded as two boxes (columns 0-31 and 32-63).
+bool make_f32_map(CUtensorMap *m, const void *base, int64_t B, int64_t H, int64_t S,
+                  const Strides3 &st, int box_rows);
+
 }  // namespace wfattn

@@ -221,7 +221,10 @@ wfattn_status_t wfattn_prefill(int dtype, int64_t batch, int64_t heads, int64_t 
   cudaError_t err;
   if (dtype == WFATTN_DTYPE_F32) {
     if (head_dim > 256) return fail(WFATTN_UNSUPPORTED, "f32 path supports head_dim <= 256");
-    err = launch_prefill_f32(a, dev, s);
+    // head_dim 64 with 16-byte aligned rows: the tensor-core kernel (3xTF32);
+    // anything else: the CUDA-core kernel.  Both hold the 1e-5 contract.
+    err = prefill_f32_tc_supported(a) ? launch_prefill_f32_tc(a, dev, s)
+                                      : launch_prefill_f32(a, dev, s);
     if (err != cudaSuccess) return cuda_fail(err, "prefill_f32 launch");
     return WFATTN_OK;
   }

@@ -66,6 +66,11 @@ struct DeviceInfo {
 cudaError_t ensure_smem_attr(const void *func, int bytes, int device);
 
 cudaError_t launch_prefill_f32(const PrefillArgs &a, const DeviceInfo &dev, cudaStream_t stream);
+// f32 prefill on the tensor cores (3xTF32 split, head_dim 64): whether the
+// views suit its TMA loads and vector stores, and its launcher.
+bool prefill_f32_tc_supported(const PrefillArgs &a);
+cudaError_t launch_prefill_f32_tc(const PrefillArgs &a, const DeviceInfo &dev,
+                                  cudaStream_t stream);
 // bf16 prefill: one 128-row query tile per CTA (2 CTAs per SM) ...
 cudaError_t launch_prefill_bf16_1q(const PrefillArgs &a, const DeviceInfo &dev,
                                    cudaStream_t stream);

@@ -74,9 +74,12 @@ struct Smem {
   uint8_t q[2][2][kTileBytes];  // [slot][tile A/B]: Q of two consecutive work items
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  // Output staging, one 32-row x 128-byte slab per softmax warp, row-major
-  // (row r at r * 128): a TMA tensor store (no swizzle) reads it for the local
-  // output and untiled bulk copies for the further destinations.
+  // Output staging, one 32-row x 128-byte slab per softmax warp (row r at
+  // r * 128).  With one destination, 16-byte chunk c of row r sits at chunk
+  // c ^ (r % 8) -- the 128-byte swizzle, read by a swizzled TMA tensor store,
+  // so that 8 threads writing their rows' chunk c hit 8 different bank groups.
+  // With further destinations (which take untiled bulk copies of the rows)
+  // the slab is plain row-major for the local TMA store too.
   uint8_t ostage[kSoftmaxWarps][32 * 128];
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
@@ -582,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive(bar_o_free);
       if (lane == 0 && (warp & 3) == (kFirstSoftmaxWarp & 3)) TL(t ? 14 : 6, k);
       const float inv = 1.f / l;
+      const uint32_t swz = p.n_remote > 0 ? 0u : (uint32_t)(lane & 7);
       // the previous item's copies must have finished reading the slab
       ptx::bulk_wait_group_read0();
       __syncwarp();
@@ -593,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         w.y = ptx::pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
         w.z = ptx::pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
         w.w = ptx::pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-        *reinterpret_cast<uint4 *>(stage + lane * 128 + (c << 4)) = w;
+        *reinterpret_cast<uint4 *>(stage + lane * 128 + (((uint32_t)c ^ swz) << 4)) = w;
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
@@ -666,11 +670,12 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
       !make_bf16_map_64x128(&tv, a.v, a.B, a.H, a.Sk, a.vs))
     return cudaErrorInvalidValue;
   // The first destination (on this GPU) takes TMA tensor stores of 32-row
-  // row-major slabs; the others, untiled bulk copies of the same slabs.
+  // slabs (128-byte swizzled when it is the only one); the others, untiled
+  // bulk copies of the same, then row-major, slabs.
   CUtensorMap to;
   if (a.n_peers > kMaxOutputPeers ||
       !make_bf16_map(&to, a.n_peers > 0 ? a.o_peers[0] : a.o, a.B, a.H, a.Sq, a.os, 64, 32,
-                     false))
+                     /*swizzle128=*/a.n_peers <= 1))
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
     return cudaErrorInvalidValue;

@@ -109,11 +109,16 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 }
 
 // V_j as loaded (row = key, 64 dims) -> V_j^T hi and lo (row = dim, 64 keys),
-// 4 x 4 blocks per thread.
+// 4 x 4 blocks per thread.  16-byte accesses are served 8 threads at a time;
+// the 8 threads t of group g take key quad 8 (g & 1) + t and dim quad
+// 8 ((g >> 1) & 1) + (t ^ (g >> 2)) -- a diagonal, so their loads (rows = keys)
+// and their transposed stores (rows = dims) each fall on the 8 distinct
+// swizzle chunk positions (bank groups) of a 128-byte row: no bank conflicts.
 __device__ __forceinline__ void transpose_split_v(const uint8_t *v, uint8_t *vt_hi,
                                                   uint8_t *vt_lo, int tid) {
   for (int blk = tid; blk < 256; blk += kSplitThreads) {
-    const int k0 = (blk >> 4) * 4, d0 = (blk & 15) * 4;
+    const int g = blk >> 3, t = blk & 7;
+    const int k0 = 4 * (8 * (g & 1) + t), d0 = 4 * (8 * ((g >> 1) & 1) + (t ^ (g >> 2)));
     float4 r[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) r[i] = *reinterpret_cast<const float4 *>(v + sw128_off(k0 + i, d0));

@@ -1078,9 +1078,11 @@ def main() -> None:
                     help="timed generations of the GPT-2 workloads (at most --steps)")
     ap.add_argument("--shape", default=None,
                     help="B,H,S override of a prefill workload (profiling a smaller case)")
-    ap.add_argument("--transport", choices=["auto", "peer", "nccl"], default="auto",
-                    help="sharded prefill's gather: the kernel stores into every rank's buffer "
-                         "over CUDA IPC mappings (peer) or chunked NCCL all-gathers")
+    ap.add_argument("--transport", choices=["auto", "multicast", "peer", "nccl"], default="auto",
+                    help="sharded prefill's gather: the kernel writes each output tile once "
+                         "through an NVLS multicast address (multicast), stores into every "
+                         "rank's buffer over CUDA IPC mappings (peer), or chunked NCCL "
+                         "all-gathers; auto takes the first of these that every rank can use")
     ap.add_argument("--chunks", type=int, default=0,
                     help="head chunks per rank for the sharded prefill's gather overlap "
                          "(0: the library default)")

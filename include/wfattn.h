@@ -133,6 +133,31 @@ WFATTN_API wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, i
                                                  float scale, int causal, void *stream);
 
 /*
+ * bf16 prefill whose output is written through a multicast (NVLS) address --
+ * the same fused all-gather as wfattn_prefill_gather, with each output byte
+ * leaving the GPU once: the NVLink switch copies it into every GPU's buffer.
+ * No counterpart in the reference.
+ *
+ * Same arguments as wfattn_prefill with dtype WFATTN_DTYPE_BF16, except that
+ * o_multicast is the multicast mapping, on the calling GPU, of a [B, H, Sq,
+ * 64] bf16 view (strides o_strides) that every participating GPU has bound to
+ * the same multicast object at the same offset (e.g. this rank's heads inside
+ * a symmetric-memory output buffer); it must be 16-byte aligned.  q, k, v must
+ * be device memory of the calling GPU (WFATTN_INVALID_ARG otherwise).  Each
+ * finished 32-row output slab is written with multimem.st (16 bytes a thread,
+ * weak, followed by a system-scope fence at the end of each thread); the
+ * stores are complete when the kernel is, and the caller synchronises with the
+ * other GPUs before they read their buffers.
+ */
+WFATTN_API wfattn_status_t wfattn_prefill_multicast(int64_t batch, int64_t heads, int64_t seq_q,
+                                                    int64_t seq_k, int64_t head_dim,
+                                                    const void *q, const int64_t *q_strides,
+                                                    const void *k, const int64_t *k_strides,
+                                                    const void *v, const int64_t *v_strides,
+                                                    void *o_multicast, const int64_t *o_strides,
+                                                    float scale, int causal, void *stream);
+
+/*
  * Decode attention: one query token per (batch, head) against a padded KV
  * cache, split over key chunks and combined (split-KV).
  *

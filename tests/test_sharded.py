@@ -274,7 +274,10 @@ class _ShmPeerBuffer:
         dist.barrier()
 
 
-def _race_worker(rank, world, port, result_path, single_slot):
+_FAKE_MC_BASE = 1 << 44  # the fake multicast mapping's address of every rank's byte 0
+
+
+def _race_worker(rank, world, port, result_path, single_slot, transport="peer"):
     """Four steps with different inputs; rank 1 keeps reading each step's output for a while
     (a slow consumer) while rank 0 runs ahead into the next step."""
     import time
@@ -302,15 +305,32 @@ def _race_worker(rank, world, port, result_path, single_slot):
             off = (ptr - m.data_ptr()) // m.element_size()
             torch.as_strided(m, q.shape, (*out_strides, 1), off).copy_(q)
 
+    def fake_mc_buffer(shape, dtype, device, group):
+        buf = _ShmPeerBuffer(shape, dtype, device, group, root)
+        maps.extend(buf.maps)
+        return buf.tensor, buf, _FAKE_MC_BASE
+
+    def fake_multicast(q, k, v, out_mc, out_strides, *, causal, scale):
+        # the "kernel": one store through the multicast address lands in every rank's buffer
+        for m in maps:
+            off = (out_mc - _FAKE_MC_BASE) // m.element_size()
+            torch.as_strided(m, q.shape, (*out_strides, 1), off).copy_(q)
+
     sharded._peer_capable = lambda device, dtype, head_dim: True
     sharded._peer_buffer = fake_buffer
     sharded._launch_gather = fake_gather
+    sharded._multicast_capable = lambda device: True
+    sharded._multicast_buffer = fake_mc_buffer
+    sharded._launch_multicast = fake_multicast
     b, h, s, d = 2, 4, 16, 64
     sp = sharded.ShardedPrefill(b, h, s, d, dtype=torch.bfloat16, device=torch.device("cpu"),
-                                transport="peer")
-    assert sp.transport == "peer"
+                                transport=transport)
+    assert sp.transport == transport
     if single_slot:  # the layout without double buffering: every call writes one slot
-        sp.peer_outs = (sp.peer_outs[0], sp.peer_outs[0])
+        if transport == "peer":
+            sp.peer_outs = (sp.peer_outs[0], sp.peer_outs[0])
+        else:
+            sp.mc_outs = (sp.mc_outs[0], sp.mc_outs[0])
         sp.slots = (sp.slots[0], sp.slots[0])
     report = []
     for step in range(4):
@@ -327,22 +347,33 @@ def _race_worker(rank, world, port, result_path, single_slot):
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["peer", "multicast"])
 @pytest.mark.parametrize("single_slot", [False, True])
-def test_peer_output_survives_a_rank_running_ahead(tmp_path, single_slot):
-    """The peer transport's output of call n must stay intact on a slow rank while a fast
-    rank runs call n+1 (its stores go to the other slot) until the slow rank's next call.
-    The single-slot layout is run too, to show the test sees the overwrite it guards
-    against."""
+def test_peer_output_survives_a_rank_running_ahead(tmp_path, single_slot, transport):
+    """The peer and multicast transports' output of call n must stay intact on a slow rank
+    while a fast rank runs call n+1 (its stores go to the other slot) until the slow rank's
+    next call.  The single-slot layout is run too, to show the test sees the overwrite it
+    guards against."""
     port = _free_port()
     path = str(tmp_path / "res")
-    mp.start_processes(_race_worker, args=(2, port, path, single_slot), nprocs=2, join=True,
-                       start_method="spawn")
+    mp.start_processes(_race_worker, args=(2, port, path, single_slot, transport), nprocs=2,
+                       join=True, start_method="spawn")
     slow = open(f"{path}.1.status").read().split()
     fast = open(f"{path}.0.status").read().split()
     # step:<result right when first read><still intact after the slow read>
-    assert [r[2] for r in slow] == ["1"] * 4
-    assert [r[2] for r in fast] == ["1"] * 4
     if single_slot:
-        assert "0" in [r[3] for r in slow[:3]], slow  # rank 0's next call overwrote it
+        # rank 0's next call overwrote the slow rank's output: seen when it first read it
+        # or after its slow read, depending on timing
+        assert any(r[2:4] != "11" for r in slow[:3]), slow
     else:
-        assert [r[3] for r in slow] == ["1"] * 4, slow
+        assert [r[2:4] for r in slow] == ["11"] * 4, slow
+        assert [r[2] for r in fast] == ["1"] * 4, fast
+
+
+def test_multicast_transport_needs_cuda_bf16_and_ranks():
+    from warpforth_b200 import sharded
+
+    assert sharded._multicast_capable("cpu") is False
+    with pytest.raises(ValueError, match="multicast transport needs"):
+        sharded.ShardedPrefill(1, 2, 8, 64, dtype=torch.bfloat16, device=torch.device("cpu"),
+                               transport="multicast")

@@ -19,7 +19,8 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 
 EXPORTED_SYMBOLS = (
     "wfattn_version", "wfattn_status_string", "wfattn_last_error", "wfattn_attention",
-    "wfattn_prefill", "wfattn_prefill_gather", "wfattn_decode_workspace_size", "wfattn_decode",
+    "wfattn_prefill", "wfattn_prefill_gather", "wfattn_prefill_multicast",
+    "wfattn_decode_workspace_size", "wfattn_decode",
     "wfattn_decode_f32_workspace_size", "wfattn_decode_f32", "wfattn_decode_noalloc", "wfattn_device_status", "wfattn_peer_alloc", "wfattn_peer_open",
     "wfattn_peer_close", "wfattn_peer_free",
 )
@@ -72,6 +73,8 @@ def load() -> ctypes.CDLL:
     lib.wfattn_prefill_gather.argtypes = [_i64, _i64, _i64, _i64, _i64, _vp, _i64p, _vp, _i64p,
                                           _vp, _i64p, ctypes.POINTER(_vp), ctypes.c_int, _i64p,
                                           ctypes.c_float, ctypes.c_int, _vp]
+    lib.wfattn_prefill_multicast.restype = ctypes.c_int
+    lib.wfattn_prefill_multicast.argtypes = lib.wfattn_prefill.argtypes[1:]
     lib.wfattn_decode_workspace_size.restype = ctypes.c_size_t
     lib.wfattn_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64]
     lib.wfattn_decode.restype = ctypes.c_int

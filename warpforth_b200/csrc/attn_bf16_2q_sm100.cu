@@ -27,7 +27,11 @@
 //                     the same lane queues bulk copies of the slab to every
 //                     further destination (other GPUs' buffers), so the TMA
 //                     engine, not the softmax warp, moves those bytes over
-//                     NVLink while the next item computes.
+//                     NVLink while the next item computes.  With a multicast
+//                     output instead, the warp reads the slab back in 512-byte
+//                     runs and writes each 16 bytes once through the multicast
+//                     address (multimem.st): the NVLink switch delivers them
+//                     to every GPU's buffer, this one's included.
 //
 // TMEM (512 columns): S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384)
 //                     O_A [384,448) O_B [448,512).
@@ -103,6 +107,9 @@ struct Params {
   // this one), written by untiled bulk copies; strides os_* are shared.
   char *remote[kMaxOutputPeers - 1];
   int n_remote;
+  // Multicast address of the output (replaces the TMA store and the remote
+  // copies when set).
+  char *mc;
   int64_t os_b, os_h, os_s;
   float scale_log2;
   int causal;
@@ -602,9 +609,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::fence_proxy_async_smem();
       __syncwarp();
       const int64_t row0 = q_tile + 32 * (warp & 3);
-      if (lane == 0)
+      if (lane == 0 && p.mc == nullptr)
         ptx::tma_store_4d(&tm_o, ptx::smem_u32(stage), 0, (int)row0, it.h, it.b);
-      if (p.n_remote > 0) {
+      if (p.mc != nullptr) {
+        // Lanes 8i..8i+7 take row 4m+i's 8 chunks in round m (the slab is
+        // swizzled: chunk c of row r at c ^ (r % 8)), so each multimem store
+        // instruction of the warp covers 4 consecutive rows.
+        const int nrows = (int)imin64(32, p.Sq - row0);
+        const int64_t head = it.b * p.os_b + it.h * p.os_h;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int r = 4 * m + (lane >> 3), c = lane & 7;
+          if (r < nrows) {
+            const uint4 w =
+                *reinterpret_cast<const uint4 *>(stage + r * 128 + ((c ^ (r & 7)) << 4));
+            ptx::multimem_st_v4(p.mc + 2 * (head + (row0 + r) * p.os_s) + 16 * c, w);
+          }
+        }
+      } else if (p.n_remote > 0) {
         // The further destinations (the all-gather of a head-sharded prefill:
         // other GPUs' buffers, written over NVLink) get the slab's valid rows
         // (those below Sq) by untiled bulk copies: one copy per destination
@@ -633,6 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Outstanding output copies must complete before the CTA exits.
     ptx::bulk_wait_group0();
+    if (p.mc != nullptr) __threadfence_system();  // multicast stores before what follows
     if (!ok) set_abort(sm);
     if (warp == kFirstSoftmaxWarp + 4 * t && lane == 0) trace(3 + t, ok ? 5 : 6);
   }
@@ -674,7 +697,8 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   // bulk copies of the same, then row-major, slabs.
   CUtensorMap to;
   if (a.n_peers > kMaxOutputPeers ||
-      !make_bf16_map(&to, a.n_peers > 0 ? a.o_peers[0] : a.o, a.B, a.H, a.Sq, a.os, 64, 32,
+      !make_bf16_map(&to, a.o_mc ? a.o_mc : a.n_peers > 0 ? a.o_peers[0] : a.o, a.B, a.H, a.Sq,
+                     a.os, 64, 32,
                      /*swizzle128=*/a.n_peers <= 1))
     return cudaErrorInvalidValue;
   if (a.B > 0x7fffffff || a.H > 0x7fffffff || a.Sk > 0x7fffffff || a.Sq > 0x7fffffff)
@@ -689,6 +713,8 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   p.Sk = a.Sk;
   p.n_pairs = (a.Sq + 2 * kBM - 1) / (2 * kBM);
   p.n_remote = a.n_peers > 1 ? a.n_peers - 1 : 0;
+  p.mc = static_cast<char *>(a.o_mc);
+  if (p.mc && p.n_remote) return cudaErrorInvalidValue;  // one output mode per launch
   for (int d = 0; d < kMaxOutputPeers - 1; ++d)
     p.remote[d] = d < p.n_remote ? static_cast<char *>(a.o_peers[d + 1]) : nullptr;
   p.os_b = a.os.b;

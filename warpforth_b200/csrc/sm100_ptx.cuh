@@ -274,6 +274,16 @@ __device__ __forceinline__ void mma_ts_lh(uint32_t d_tmem, uint32_t a_tmem, uint
       : "memory");
 }
 
+// 16 bytes through a multicast (NVLS) address: one store that the NVLink
+// switch delivers to the memory of every GPU bound to the multicast object.
+// The f32 form moves the 32-bit patterns unchanged.
+__device__ __forceinline__ void multimem_st_v4(void *addr, uint4 v) {
+  asm volatile("multimem.st.weak.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
 // kind::tf32 forms (f32 bit patterns in; the MMA uses their top 19 bits).
 __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                             uint32_t idesc, uint32_t accumulate) {

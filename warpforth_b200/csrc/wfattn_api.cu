@@ -285,6 +285,44 @@ wfattn_status_t wfattn_prefill_gather(int64_t batch, int64_t heads, int64_t seq_
   return WFATTN_OK;
 }
 
+wfattn_status_t wfattn_prefill_multicast(int64_t batch, int64_t heads, int64_t seq_q,
+                                         int64_t seq_k, int64_t head_dim, const void *q,
+                                         const int64_t *q_strides, const void *k,
+                                         const int64_t *k_strides, const void *v,
+                                         const int64_t *v_strides, void *o_multicast,
+                                         const int64_t *o_strides, float scale, int causal,
+                                         void *stream) {
+  t_last_error.clear();
+  if (!o_multicast || (reinterpret_cast<uintptr_t>(o_multicast) & 15u))
+    return fail(WFATTN_INVALID_ARG, "o_multicast must be a non-null, 16-byte aligned address");
+  PrefillArgs a;
+  DeviceInfo dev;
+  wfattn_status_t st = prepare_prefill(batch, heads, seq_q, seq_k, head_dim, q, q_strides, k,
+                                       k_strides, v, v_strides, nullptr, o_strides, scale,
+                                       causal, &a, &dev);
+  if (st != WFATTN_OK) return st;
+  a.o_mc = o_multicast;
+  st = check_bf16(a);
+  if (st != WFATTN_OK) return st;
+  // q, k, v are read through TMA tensor maps: this GPU's own memory only.
+  const void *local[3] = {q, k, v};
+  const char *names[3] = {"q", "k", "v"};
+  for (int i = 0; i < 3; ++i) {
+    cudaPointerAttributes attr;
+    const cudaError_t perr = cudaPointerGetAttributes(&attr, local[i]);
+    if (perr != cudaSuccess) {
+      cudaGetLastError();
+      return cuda_fail(perr, "cudaPointerGetAttributes");
+    }
+    if (attr.type != cudaMemoryTypeDevice || attr.device != dev.device)
+      return fail(WFATTN_INVALID_ARG, "%s must be device memory of the calling GPU (%d)",
+                  names[i], dev.device);
+  }
+  cudaError_t err = launch_prefill_bf16_2q(a, dev, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "prefill_bf16 launch");
+  return WFATTN_OK;
+}
+
 wfattn_status_t wfattn_attention(const float *Q, const float *K, const float *V, float *O,
                                  int64_t seq_len, int64_t head_dim, const wfattn_dim3 *grid,
                                  const wfattn_dim3 *block, void *stream) {

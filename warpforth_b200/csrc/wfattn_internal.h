@@ -35,6 +35,10 @@ struct PrefillArgs {
   // these buffers (same shape and strides os, possibly on other GPUs) instead of o.
   void *const *o_peers = nullptr;
   int n_peers = 0;
+  // bf16 two-tile kernel only: when set, a multicast (NVLS) address of the
+  // output (shape and strides os) bound on every GPU of the gather; each output
+  // row is written once through it and lands in every GPU's buffer.
+  void *o_mc = nullptr;
 };
 
 struct DecodeArgs {

@@ -2,9 +2,17 @@
 
 Every (batch, head) pair of attention is independent, so G ranks (one process
 per GPU) split the heads evenly and compute them with no exchange; the only
-exchange is the all-gather of O.  Two transports:
+exchange is the all-gather of O.  Three transports:
 
-* ``peer`` (bf16 on GPUs, the default there): every rank holds two full
+* ``multicast`` (bf16 on GPUs with NVLS, the default there): every rank holds
+  two full [B, H, S, D] output slots in one symmetric-memory buffer
+  (``torch.distributed._symmetric_memory``) that all ranks have bound to one
+  NVLink multicast object.  The attention kernel writes each finished output
+  tile of its heads once through the multicast address
+  (``wfattn_prefill_multicast``, ``multimem.st``) and the NVLink switch
+  delivers it to every rank's buffer: a rank's NVLink egress is its own share
+  of O, not (G - 1) copies of it.  Slots and the closing barrier as for peer.
+* ``peer`` (bf16 on GPUs without NVLS): every rank holds two full
   [B, H, S, D] output slots in one ``peer.PeerBuffer`` mapped on all ranks
   (CUDA IPC).  The attention kernel stores each finished output tile of its
   heads into every rank's buffer over NVLink (``wfattn_prefill_gather``), so
@@ -65,6 +73,46 @@ def _peer_capable(device, dtype, head_dim) -> bool:
     return torch.device(device).type == "cuda" and dtype == torch.bfloat16 and head_dim == 64
 
 
+class MulticastSetupError(RuntimeError):
+    """Some rank has no usable multicast mapping (raised on every rank)."""
+
+
+def _multicast_capable(device) -> bool:
+    """Whether torch's symmetric memory offers an NVLS multicast mapping on this device."""
+    device = torch.device(device)
+    if device.type != "cuda":
+        return False
+    try:
+        from torch.distributed._symmetric_memory import DeviceType, _SymmetricMemory
+
+        return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index or 0))
+    except (ImportError, AttributeError, RuntimeError):
+        return False
+
+
+def _multicast_buffer(shape, dtype, device, group):
+    """(this rank's buffer, a handle that keeps the mapping alive, the multicast address of
+    the buffer's first byte or 0).  Collective.  The kernel addresses the output as
+    multicast base + byte offset, so the address is given only when the tensor starts
+    its allocation: then the multicast base and this rank's buffer base describe the
+    same bytes."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    buf = symm_mem.empty(shape, dtype=dtype, device=device)
+    hdl = symm_mem.rendezvous(buf, group if group is not None else dist.group.WORLD)
+    mc = int(hdl.multicast_ptr) if hdl.multicast_ptr else 0
+    rank = dist.get_rank(group)
+    if mc % 16 or int(hdl.offset) != 0 or buf.data_ptr() != int(hdl.buffer_ptrs[rank]):
+        mc = 0
+    return buf, hdl, mc
+
+
+def _launch_multicast(q, k, v, out_mc, out_strides, *, causal, scale):
+    from .warpforth import attention_multicast_ptr
+
+    attention_multicast_ptr(q, k, v, out_mc, out_strides, causal=causal, scale=scale)
+
+
 def _peer_buffer(shape, dtype, device, group):
     from .peer import PeerBuffer
 
@@ -86,16 +134,16 @@ def _default_compute(q, k, v, *, causal, scale, out):
 class ShardedPrefill:
     """Runs this rank's share of a [B, H, S, D] attention and all-gathers O.
 
-    The output buffers (two slots of [B, H, S, D] for the peer transport,
+    The output buffers (two slots of [B, H, S, D] for the multicast and peer transports,
     ``gathered`` = [C, G, h, B, S, D] for NCCL) are allocated once and reused.
     ``__call__`` takes this rank's q/k/v as per-chunk lists of [B, h, S, D]
     views (from ``shard`` of the full tensors or ``split_local`` of a
-    rank-local tensor; one chunk with the peer transport) and returns the full
-    [B, H, S, D] output.  ``transport`` is "auto" (peer where possible), "peer"
-    or "nccl".
+    rank-local tensor; one chunk with multicast or peer) and returns the full
+    [B, H, S, D] output.  ``transport`` is "auto" (multicast, else peer, where
+    possible), "multicast", "peer" or "nccl".
 
     Lifetime of the returned tensor: it holds this call's output until the
-    call after next (peer transport: the two slots alternate; NCCL: the
+    call after next (multicast and peer: the two slots alternate; NCCL: the
     gather buffer is reused by the next call).  Whatever reads it must be
     queued on the current stream, or finished on the host, before this rank's
     next call; other ranks cannot overwrite it before then.
@@ -105,7 +153,7 @@ class ShardedPrefill:
                  dtype: torch.dtype, device: torch.device, group=None,
                  compute: ComputeFn | None = None, chunks: int | None = None,
                  transport: str = "auto") -> None:
-        if transport not in ("auto", "peer", "nccl"):
+        if transport not in ("auto", "multicast", "peer", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -115,11 +163,20 @@ class ShardedPrefill:
         self.B, self.H, self.S, self.D = batch, heads, seq, head_dim
         self.transport = "nccl"
         self.peer = None
+        self.mc_buf = self.mc_handle = None
         peer_ok = (self.world > 1 and _peer_capable(device, dtype, head_dim)
                    and compute is None and chunks in (None, 1))
-        if transport == "peer" and not peer_ok:
-            raise ValueError("the peer transport needs bf16, head_dim 64, CUDA and >1 rank")
-        if transport in ("auto", "peer") and peer_ok:
+        if transport in ("peer", "multicast") and not peer_ok:
+            raise ValueError(f"the {transport} transport needs bf16, head_dim 64, CUDA and "
+                             ">1 rank")
+        if transport in ("auto", "multicast") and peer_ok:
+            try:  # collective; every rank agrees before and after the rendezvous
+                self._setup_multicast(dtype, device)
+                self.transport = "multicast"
+            except MulticastSetupError:
+                if transport == "multicast":
+                    raise
+        if self.transport == "nccl" and transport in ("auto", "peer") and peer_ok:
             from .peer import PeerSetupError
 
             try:  # collective; on failure every rank raises, so all of them fall back
@@ -128,7 +185,7 @@ class ShardedPrefill:
             except PeerSetupError:
                 if transport == "peer":
                     raise
-        if self.transport == "peer":
+        if self.transport in ("multicast", "peer"):
             self.chunks, self.ch = 1, self.local_heads
             return
         self.chunks = chunks or default_chunks(heads, self.world)
@@ -138,6 +195,28 @@ class ShardedPrefill:
         self.gathered = torch.empty((self.chunks, self.world, self.ch, batch, seq, head_dim),
                                     dtype=dtype, device=device)
         self.compute = compute or _default_compute
+
+    def _agree(self, ok: bool, device) -> bool:
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(int(flag.item()))
+
+    def _setup_multicast(self, dtype, device) -> None:
+        if not self._agree(_multicast_capable(device), device):
+            raise MulticastSetupError("no NVLS multicast support on some rank")
+        buf, hdl, mc = _multicast_buffer((2, self.B, self.H, self.S, self.D), dtype, device,
+                                         self.group)
+        if not self._agree(mc != 0, device):
+            raise MulticastSetupError("no multicast address at the start of the output buffer")
+        self.mc_buf, self.mc_handle = buf, hdl
+        self.slots = (buf[0], buf[1])
+        esz = buf.element_size()
+        head_off = self.rank * self.local_heads * buf.stride(2) * esz
+        slot_bytes = buf.stride(0) * esz
+        self.mc_outs = tuple(mc + s * slot_bytes + head_off for s in (0, 1))
+        self.out_strides = buf.stride()[1:4]
+        self.calls = 0
+        self._sync = torch.zeros(1, dtype=torch.int32, device=device)
 
     def _setup_peer(self, dtype, device) -> None:
         # two output slots [2, B, H, S, D] in one buffer per rank, mapped on every rank
@@ -164,6 +243,13 @@ class ShardedPrefill:
             self.slots = None
             self.peer.close()
             self.peer = None
+        if self.transport == "multicast" and self.mc_buf is not None:
+            # no rank may still write through the multicast mapping when it goes
+            if self.mc_buf.device.type == "cuda":
+                torch.cuda.synchronize(self.mc_buf.device)
+            dist.all_reduce(self._sync, group=self.group)
+            self.slots = None
+            self.mc_handle = self.mc_buf = None
 
     def chunk_heads(self, c: int) -> tuple[int, int]:
         """Global head range of this rank's part of chunk c."""
@@ -181,7 +267,7 @@ class ShardedPrefill:
 
     def output_view(self) -> torch.Tensor:
         """The full [B, H, S, D] output of the last call."""
-        if self.transport == "peer":
+        if self.transport in ("multicast", "peer"):
             return self.slots[(self.calls - 1) & 1]
         return self.gathered.view(self.H, self.B, self.S, self.D).permute(1, 0, 2, 3)
 
@@ -193,9 +279,13 @@ class ShardedPrefill:
     def compute_local(self, qs: Sequence[torch.Tensor], ks: Sequence[torch.Tensor],
                       vs: Sequence[torch.Tensor], *, causal: bool = True,
                       scale: float | None = None) -> None:
-        """This rank's heads only, without the final synchronisation (peer transport: the
+        """This rank's heads only, without the final synchronisation (multicast and peer: the
         kernel still stores into every rank's buffer, into the slot the next call
         writes)."""
+        if self.transport == "multicast":
+            _launch_multicast(qs[0], ks[0], vs[0], self.mc_outs[self.calls & 1],
+                              self.out_strides, causal=causal, scale=scale)
+            return
         if self.transport == "peer":
             _launch_gather(qs[0], ks[0], vs[0], self.peer_outs[self.calls & 1],
                            self.out_strides, causal=causal, scale=scale)
@@ -206,7 +296,7 @@ class ShardedPrefill:
     def __call__(self, qs: Sequence[torch.Tensor], ks: Sequence[torch.Tensor],
                  vs: Sequence[torch.Tensor], *, causal: bool = True,
                  scale: float | None = None) -> torch.Tensor:
-        if self.transport == "peer":
+        if self.transport in ("multicast", "peer"):
             self.compute_local(qs, ks, vs, causal=causal, scale=scale)
             self.calls += 1
             # A one-element NCCL all-reduce as the cross-rank barrier: once it is

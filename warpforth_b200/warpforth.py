@@ -157,6 +157,26 @@ def attention_gather_ptrs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         1 if causal else 0, _stream_handle(q.device)))
 
 
+def attention_multicast_ptr(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out_mc: int,
+                            out_strides: tuple[int, int, int], *, causal: bool = True,
+                            scale: float | None = None) -> None:
+    """bf16 prefill whose output goes out through a multicast (NVLS) address: ``out_mc`` is
+    the start, in this GPU's multicast mapping, of a [B, H, Sq, 64] bf16 view with element
+    strides ``out_strides`` = (batch, head, seq) that every rank has bound at the same
+    offset (this rank's heads inside a symmetric-memory buffer).  Each output row leaves
+    the GPU once and lands in every rank's buffer; q, k and v must be this GPU's memory.
+    The stores are complete when the kernel is; the caller synchronises with the other
+    ranks afterwards."""
+    _check_bf16_qkv(q, k, v)
+    b, h, sq, d = q.shape
+    lib = _lib.load()
+    st = [_lib.strides_arg(t.stride()[:3]) for t in (q, k, v)]
+    _lib.check(lib.wfattn_prefill_multicast(
+        b, h, sq, k.shape[2], d, _ptr(q), st[0], _ptr(k), st[1], _ptr(v), st[2],
+        ctypes.c_void_p(out_mc), _lib.strides_arg(out_strides), float(scale) if scale else 0.0,
+        1 if causal else 0, _stream_handle(q.device)))
+
+
 class DecodeWorkspace:
     """Caller-owned scratch for ``decode`` (grown on demand, reused across calls)."""
 

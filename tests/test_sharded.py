@@ -377,3 +377,39 @@ def test_multicast_transport_needs_cuda_bf16_and_ranks():
     with pytest.raises(ValueError, match="multicast transport needs"):
         sharded.ShardedPrefill(1, 2, 8, 64, dtype=torch.bfloat16, device=torch.device("cpu"),
                                transport="multicast")
+
+
+def _mc_fallback_worker(rank, world, port, result_path):
+    """auto transport where rank 1 cannot set up its multicast buffer: every rank must end up
+    on the peer transport."""
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
+    from warpforth_b200 import sharded
+
+    root = os.path.dirname(result_path)
+
+    def fake_mc_buffer(shape, dtype, device, group):
+        if rank == 1:
+            raise RuntimeError("no multicast object for this rank")
+        return torch.empty(shape, dtype=dtype), None, _FAKE_MC_BASE
+
+    sharded._peer_capable = lambda device, dtype, head_dim: True
+    sharded._multicast_capable = lambda device: True
+    sharded._multicast_buffer = fake_mc_buffer
+    sharded._peer_buffer = lambda shape, dtype, device, group: _ShmPeerBuffer(
+        shape, dtype, device, group, root)
+    sp = sharded.ShardedPrefill(2, 4, 16, 64, dtype=torch.bfloat16, device=torch.device("cpu"))
+    with open(f"{result_path}.{rank}.status", "w") as f:
+        f.write(sp.transport)
+    sp.close()
+    dist.destroy_process_group()
+
+
+def test_multicast_setup_failure_on_one_rank_falls_back_to_peer_everywhere(tmp_path):
+    path = str(tmp_path / "res")
+    mp.start_processes(_mc_fallback_worker, args=(2, _free_port(), path), nprocs=2, join=True,
+                       start_method="spawn")
+    assert [open(f"{path}.{r}.status").read() for r in range(2)] == ["peer", "peer"]

@@ -204,8 +204,12 @@ class ShardedPrefill:
     def _setup_multicast(self, dtype, device) -> None:
         if not self._agree(_multicast_capable(device), device):
             raise MulticastSetupError("no NVLS multicast support on some rank")
-        buf, hdl, mc = _multicast_buffer((2, self.B, self.H, self.S, self.D), dtype, device,
-                                         self.group)
+        try:
+            buf, hdl, mc = _multicast_buffer((2, self.B, self.H, self.S, self.D), dtype, device,
+                                             self.group)
+        except RuntimeError:  # this rank could not allocate or map; all ranks learn it next
+            buf = hdl = None
+            mc = 0
         if not self._agree(mc != 0, device):
             raise MulticastSetupError("no multicast address at the start of the output buffer")
         self.mc_buf, self.mc_handle = buf, hdl

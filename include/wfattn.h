@@ -94,7 +94,11 @@ WFATTN_API wfattn_status_t wfattn_attention(const float *Q, const float *K, cons
  * `attention` launch per head, batch index 0 only) with one call over all
  * batches and heads, reading the strided q/k/v views directly.
  *
- * dtype WFATTN_DTYPE_F32: q, k, v, o are f32; any head_dim in [1, 256].
+ * dtype WFATTN_DTYPE_F32: q, k, v, o are f32; any head_dim in [1, 256].  With
+ *   head_dim 64, 16-byte aligned pointers, strides that are multiples of 4
+ *   elements and no zero (broadcast) strides, it runs on the tensor cores
+ *   (three tf32 MMAs per product); otherwise on the CUDA cores.  Both stay
+ *   within 1e-5 absolute of the f64 reference.
  * dtype WFATTN_DTYPE_BF16: q, k, v, o are bf16; head_dim must be 64; the
  *   q/k/v base pointers must be 16-byte aligned and their batch/head/seq
  *   strides multiples of 8 elements (TMA requirements).

@@ -73,8 +73,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool
 
     q is [B, H, Sq, D], k and v are [B, H, Sk, D]; any batch/head/seq strides
     are accepted (the head_dim stride must be 1).  f32 tensors run the
-    reference-accurate CUDA-core kernel (head_dim <= 256); bf16 tensors run
-    the tcgen05 tensor-core kernel (head_dim 64).  Causal masking aligns the
+    reference-accurate path (head_dim <= 256; within 1e-5 of f64): the 3xTF32
+    tensor-core kernel for head_dim 64 with 16-byte aligned rows, the CUDA-core
+    kernel otherwise; bf16 tensors run the tcgen05 tensor-core kernel (head_dim 64).  Causal masking aligns the
     queries with the end of the keys.  Returns ``out`` (allocated as a
     contiguous [B, H, Sq, D] tensor of q's dtype when not given).
     """

@@ -629,6 +629,20 @@ def run_prefill(args, ctx: Ctx, w: Workload) -> dict:
         torch.cuda.synchronize()
         kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
         ctx.barrier()
+        # the same heads computed into a local buffer, with no gather at all: what the
+        # rank's kernel would take if nothing had to cross NVLink
+        local_out = torch.empty((w.B, sp.local_heads, w.S, w.D), dtype=tdt, device=dev)
+        outs = sp.split_local(local_out)
+        ev = [(ctx.event(), ctx.event()) for _ in range(args.steps)]
+        for a, b in ev:
+            a.record(ctx.stream)
+            for c in range(sp.chunks):
+                wf.attention(qs[c], ks[c], vs[c], out=outs[c])
+            b.record(ctx.stream)
+        torch.cuda.synchronize()
+        compute_ms = ctx.max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev))
+        del local_out, outs
+        ctx.barrier()
     total_ms = ctx.max_over_ranks(total_ms)
     kernel_ms = ctx.max_over_ranks(kernel_ms)
     ms_per_step = total_ms / args.steps
@@ -727,6 +741,24 @@ def run_prefill(args, ctx: Ctx, w: Workload) -> dict:
     }
     if parity is not None:
         line["parity"] = parity
+    if sp is not None and world > 1:
+        # NVLink volume of the gather per rank and step; the fused kernel can finish no
+        # sooner than the slower of its compute alone and its link time at the measured
+        # 770 GB/s per direction of a peer copy
+        share = w.B * sp.local_heads * w.S * w.D * (2 if tdt == torch.bfloat16 else 4)
+        others = share * (world - 1)
+        link_ms = others / 770e9 * 1e3
+        line["gather"] = {
+            "transport": sp.transport,
+            "bytes_in_per_rank": others, "bytes_out_per_rank":
+                share if sp.transport == "multicast" else others,
+            "compute_only_ms": compute_ms, "fused_kernel_ms": kernel_ms,
+            "link_bound_ms": link_ms, "link_gbs": 770.0,
+            "fused_frac": max(compute_ms, link_ms) / kernel_ms,
+            "what": "bytes_in: the other ranks' shares of O; bytes_out: this rank's share, once "
+                    "(multicast: the NVLink switch replicates it, its own copy included) or once "
+                    "per other rank; compute_only: this rank's heads into a local buffer; "
+                    "fused_frac = max(compute_only, link_bound) / fused kernel"}
     if not w.sharded and w.dtype == "f32" and ctx.rank == 0:
         line["reference_ptx"] = ref_ptx_prefill(ctx, w, q, k, v, out, args)
     if sp is not None:

@@ -31,7 +31,26 @@ K_STAGES = 3
 BM = 128  # rows per query tile; keys per K/V tile
 
 
-def item_order(sq: int, sk: int, bh: int, grid: int, cta: int, causal: bool) -> list[list[int]]:
+def item_indices(n_items: int, blocks: int, cta: int, interleave: bool = False) -> list[int]:
+    """Indices (in the heaviest-first order) of the items CTA `cta` takes, in its order: round
+    k's item of this CTA, snake-wise; with `interleave` (the kernel's gather modes) the full
+    rounds alternate between the heavy and the light end, a partial last round last."""
+    full = n_items // blocks
+    out = []
+    k = 0
+    while True:
+        r = k
+        if interleave and r < full:
+            r = full - 1 - (r >> 1) if (r & 1) else (r >> 1)
+        idx = r * blocks + ((blocks - 1 - cta) if (k & 1) else cta)
+        if idx >= n_items:
+            return out
+        out.append(idx)
+        k += 1
+
+
+def item_order(sq: int, sk: int, bh: int, grid: int, cta: int, causal: bool,
+               interleave: bool = False) -> list[list[int]]:
     """nkv = [key tiles of tile A, of tile B] for each item of CTA `cta`, in its order."""
     n_pairs = (sq + 2 * BM - 1) // (2 * BM)
     n_items = n_pairs * bh
@@ -39,11 +58,7 @@ def item_order(sq: int, sk: int, bh: int, grid: int, cta: int, causal: bool) -> 
     group = 8 if (n_pairs >= 16 and n_items >= 32 * blocks) else 1
     off = sk - sq
     out = []
-    k = 0
-    while True:
-        idx = k * blocks + ((blocks - 1 - cta) if (k & 1) else cta)
-        if idx >= n_items:
-            return out
+    for idx in item_indices(n_items, blocks, cta, interleave):
         n_full = n_pairs // group
         if idx < n_full * group * bh:
             g, r = divmod(idx, group * bh)
@@ -60,7 +75,23 @@ def item_order(sq: int, sk: int, bh: int, grid: int, cta: int, causal: bool) -> 
             kend = min(sk, r0 + rows + off) if (causal and rows > 0) else sk
             nkv.append((kend + BM - 1) // BM if rows > 0 else 0)
         out.append(nkv)
-        k += 1
+    return out
+
+
+@pytest.mark.parametrize("n_items,blocks", [(384, 148), (3072, 148), (148, 148), (100, 148),
+                                            (1000, 148), (296, 148), (3, 1)])
+@pytest.mark.parametrize("interleave", [False, True])
+def test_item_order_covers_every_item_once(n_items, blocks, interleave):
+    seen = sorted(i for c in range(blocks) for i in item_indices(n_items, blocks, c, interleave))
+    assert seen == list(range(n_items))
+
+
+def test_interleaved_rounds_alternate_heavy_and_light():
+    # 5 full rounds of 148 and a partial one of 20: 0, 4, 1, 3, 2, then the partial round 5,
+    # whose items go (snake order, reversed in odd rounds) to the last 20 CTAs
+    rounds = [[i // 148 for i in item_indices(5 * 148 + 20, 148, c, interleave=True)]
+              for c in (0, 147)]
+    assert rounds == [[0, 4, 1, 3, 2], [0, 4, 1, 3, 2, 5]]
 
 
 class ProtocolError(AssertionError):
@@ -308,11 +339,12 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("interleave", [False, True])
 @pytest.mark.parametrize("sq,sk,bh,causal", CASES)
-def test_two_tile_kernel_protocol(sq, sk, bh, causal):
+def test_two_tile_kernel_protocol(sq, sk, bh, causal, interleave):
     grid = min(148, ((sq + 255) // 256) * bh)
     for cta in sorted({0, 1, grid // 2, grid - 1}):
-        items = item_order(sq, sk, bh, grid, cta, causal)[:10]
+        items = item_order(sq, sk, bh, grid, cta, causal, interleave)[:10]
         for seed in range(12):
             simulate(items, seed)
 

@@ -110,6 +110,7 @@ struct Params {
   // Multicast address of the output (replaces the TMA store and the remote
   // copies when set).
   char *mc;
+  int interleave;  // heavy and light rounds alternate (item_of)
   int64_t os_b, os_h, os_s;
   float scale_log2;
   int causal;
@@ -133,7 +134,16 @@ struct Item {
 __device__ __forceinline__ bool item_of(const Params &p, int k, Item &it) {
   // 32-bit arithmetic: the launcher keeps n_items below 2^31.
   const uint32_t G = gridDim.x;
-  const uint32_t idx = (uint32_t)k * G + ((k & 1) ? G - 1 - blockIdx.x : blockIdx.x);
+  // Round r of the heaviest-first order holds items r*G .. r*G+G-1.  When the
+  // kernel also sends its output to other GPUs, the CTAs take the full rounds
+  // alternately from the heavy and the light end (0, F-1, 1, F-2, ...; a
+  // partial last round stays last): every item writes the same bytes whatever
+  // its length, so in plain order the light items at the end would produce
+  // output faster than NVLink takes it.
+  uint32_t r = (uint32_t)k;
+  const uint32_t F = (uint32_t)p.n_items / G;
+  if (p.interleave && r < F) r = (r & 1) ? F - 1 - (r >> 1) : (r >> 1);
+  const uint32_t idx = r * G + ((k & 1) ? G - 1 - blockIdx.x : blockIdx.x);
   if ((int64_t)idx >= p.n_items) return false;
   const uint32_t BH = (uint32_t)(p.B * p.H), H = (uint32_t)p.H;
   const uint32_t NP = (uint32_t)p.n_pairs, gs = p.group, n_full = NP / gs;
@@ -714,6 +724,7 @@ cudaError_t launch_prefill_bf16_2q(const PrefillArgs &a, const DeviceInfo &dev,
   p.n_pairs = (a.Sq + 2 * kBM - 1) / (2 * kBM);
   p.n_remote = a.n_peers > 1 ? a.n_peers - 1 : 0;
   p.mc = static_cast<char *>(a.o_mc);
+  p.interleave = (p.mc != nullptr || p.n_remote > 0) ? 1 : 0;
   if (p.mc && p.n_remote) return cudaErrorInvalidValue;  // one output mode per launch
   for (int d = 0; d < kMaxOutputPeers - 1; ++d)
     p.remote[d] = d < p.n_remote ? static_cast<char *>(a.o_peers[d + 1]) : nullptr;

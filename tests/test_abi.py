@@ -109,25 +109,28 @@ def _integration_blocks(lang: str) -> list[str]:
     return re.findall(rf"```{lang}\n(.*?)```", (ROOT / "INTEGRATION.md").read_text(), re.S)
 
 
-def test_integration_c_example_compiles(tmp_path):
-    """The multi-GPU C example (peer buffers + wfattn_prefill_gather) compiles as written."""
+def test_integration_c_examples_compile(tmp_path):
+    """The multi-GPU C examples (multicast: wfattn_prefill_multicast; peer buffers:
+    wfattn_prefill_gather) compile as written."""
     import shutil
     import subprocess
 
     if shutil.which("gcc") is None:
         pytest.skip("no C compiler")
-    (block,) = _integration_blocks("c")
-    src = tmp_path / "example.c"
-    src.write_text(
-        "#include <stdint.h>\n#include \"wfattn.h\"\n"
-        "void step(int64_t B, int64_t H, int64_t S, int G, int rank, int dev,\n"
-        "          const void *q_local, const int64_t *q_strides, const void *k_local,\n"
-        "          const int64_t *k_strides, const void *v_local, const int64_t *v_strides,\n"
-        "          void *stream) {\n" + block + "}\n")
-    res = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-Wno-unused-result", "-c",
-                          "-I", str(ROOT / "include"), str(src), "-o", str(tmp_path / "e.o")],
-                         capture_output=True, text=True)
-    assert res.returncode == 0, res.stderr
+    blocks = _integration_blocks("c")
+    assert len(blocks) == 2
+    for i, block in enumerate(blocks):
+        src = tmp_path / f"example{i}.c"
+        src.write_text(
+            "#include <stdint.h>\n#include \"wfattn.h\"\n"
+            "void step(int64_t B, int64_t H, int64_t S, int G, int rank, int dev, void *mc,\n"
+            "          int slot, const void *q_local, const int64_t *q_strides,\n"
+            "          const void *k_local, const int64_t *k_strides, const void *v_local,\n"
+            "          const int64_t *v_strides, void *stream) {\n" + block + "}\n")
+        res = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-Wno-unused-result", "-c",
+                              "-I", str(ROOT / "include"), str(src),
+                              "-o", str(tmp_path / f"e{i}.o")], capture_output=True, text=True)
+        assert res.returncode == 0, res.stderr
 
 
 def test_integration_python_binding_reports_errors():

@@ -432,7 +432,10 @@ struct CombineParams {
   int64_t os_b, os_h;
 };
 
-// One warp per (batch, head): merge the chunk partials, write f32 output.
+// One warp per (batch, head): merge the chunk partials, write f32 output.  The
+// partials are independent loads: lane c takes chunk c's (m, l) in one round
+// trip, and the column sums issue eight chunks' loads before using any, so a
+// row costs a few L2 round trips rather than one per chunk.
 template <int kChunk>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams p) {
   const int lane = threadIdx.x & 31;
@@ -448,15 +451,34 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
   float o0 = 0.f, o1 = 0.f, l = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    const float *pc = part + (size_t)c * kPartFloats;
-    const float mc = pc[kD];
-    const float w = mc == -INFINITY ? 0.f : ptx::ex2_approx(mc - M);
-    const float2 a = *reinterpret_cast<const float2 *>(pc + 2 * lane);
-    o0 = fmaf(a.x, w, o0);
-    o1 = fmaf(a.y, w, o1);
-    l = fmaf(pc[kD + 1], w, l);
+  for (int c0 = 0; c0 < nc; c0 += 32) {
+    // lane i: weight and sum of chunk c0 + i
+    const int ci = c0 + lane;
+    float w = 0.f;
+    if (ci < nc) {
+      const float *pc = part + (size_t)ci * kPartFloats;
+      const float mc = pc[kD];
+      w = mc == -INFINITY ? 0.f : ptx::ex2_approx(mc - M);
+      l = fmaf(pc[kD + 1], w, l);
+    }
+    const int cnt = nc - c0 < 32 ? nc - c0 : 32;
+    for (int i = 0; i < cnt; i += 8) {
+      float2 a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        a[u] = i + u < cnt ? *reinterpret_cast<const float2 *>(
+                                 part + (size_t)(c0 + i + u) * kPartFloats + 2 * lane)
+                           : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wu = __shfl_sync(0xffffffffu, w, (i + u) & 31);
+        o0 = fmaf(a[u].x, wu, o0);
+        o1 = fmaf(a[u].y, wu, o1);
+      }
+    }
   }
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) l += __shfl_xor_sync(0xffffffffu, l, sh);
   const float inv = l > 0.f ? 1.f / l : 0.f;
   float *dst = p.o + b * p.os_b + h * p.os_h;
   *reinterpret_cast<float2 *>(dst + 2 * lane) = make_float2(o0 * inv, o1 * inv);

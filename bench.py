@@ -723,7 +723,7 @@ def run_prefill(args, ctx: Ctx, w: Workload) -> dict:
     if traffic is not None and w.sharded:
         traffic = int(traffic * heads / w.H)  # this rank's launch
     roof.update({"achieved": achieved, "unit": "TFLOP/s", "frac": achieved / roof["peak"],
-                 "kernel_ms": kernel_ms, "traffic": traffic,
+                 "kernel_ms": kernel_ms, "traffic": traffic, "traffic_source": TRAFFIC_SOURCE,
                  "algorithmic_flop_per_launch": kernel_flops})
     line = {
         "metric": "causal SDPA TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
@@ -827,7 +827,7 @@ def run_decode(args, ctx: Ctx, w: Workload) -> dict:
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": f"{ctx.peak_src} hbm_gbs",
             "kernel": "decode_split_kernel + decode_combine_kernel (one library call)",
-            "kernel_ms": split_ms, "traffic": load_traffic(w),
+            "kernel_ms": split_ms, "traffic": load_traffic(w), "traffic_source": TRAFFIC_SOURCE,
             "algorithmic_bytes_per_launch": kv_bytes}
     return {
         "metric": "decode attention KV GB/s per B200", "value": value, "unit": "GB/s",
@@ -1155,6 +1155,10 @@ def main() -> None:
     if ctx.rank == 0:
         print(json.dumps(line), flush=True)
     ctx.close()
+
+
+TRAFFIC_SOURCE = ("dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of this "
+                  "kernel on this workload (profiles/traffic.md), not measured in this run")
 
 
 def load_traffic(w: Workload):

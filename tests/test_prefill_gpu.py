@@ -121,6 +121,23 @@ def test_f32_hf_strided_views_and_noncausal_and_cross_lengths(wf):
     assert np.abs(dst.transpose(1, 2).cpu().numpy() - ref).max() <= F32_ABS_TOL
 
 
+def test_f32_unaligned_view_takes_the_cuda_core_kernel(wf):
+    # q starts 4 bytes into its buffer: not 16-byte aligned, so the TMA-fed tensor-core
+    # kernel cannot read it and the call runs on the CUDA-core kernel, at the same contract
+    shape = (2, 3, 129, 64)
+    n = 2 * 3 * 129 * 64
+    base = _randn((n + 1,), 500).cuda()
+    q = base[1:].view(shape)
+    assert q.data_ptr() % 16 != 0
+    k, v = (_randn(shape, 501 + i).cuda() for i in range(2))
+    out = wf.attention(q, k, v).cpu().numpy()
+    ref = _oracle(q.cpu(), k.cpu(), v.cpu())
+    assert np.abs(out - ref).max() <= F32_ABS_TOL
+    # the same values from an aligned copy (tensor-core kernel) agree within the contract too
+    out_tc = wf.attention(q.clone(), k, v).cpu().numpy()
+    assert np.abs(out_tc - ref).max() <= F32_ABS_TOL
+
+
 def test_f32_gpt2_batched_config3_all_heads(wf):
     # [8, 12, 1024, 64] f32, seed 2: every row of every head against the f64 oracle
     torch.manual_seed(2)

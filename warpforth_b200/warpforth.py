@@ -25,7 +25,15 @@ def _ptr(t: torch.Tensor) -> int:
     return t.data_ptr()
 
 
+# The current stream's raw handle without building a torch.cuda.Stream object per call (the
+# accessor torch's own compiled kernels use); the public call where it is absent.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_handle(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None
+                           else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 

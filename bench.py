@@ -797,18 +797,26 @@ def run_decode(args, ctx: Ctx, w: Workload) -> dict:
     # end to end, decode serving: the KV cache is resident state; a step's inputs are the new
     # query token, the new K/V row of every (batch, head) and the lengths
     g = torch.Generator().manual_seed(w.seed + 1000)
-    q_h, knew_h, vnew_h = (torch.randn(w.B, w.H, w.D, generator=g).to(tdt).pin_memory()
-                           for _ in range(3))
-    lens_h = decode_lens().pin_memory()
-    qn, knew, vnew = (torch.empty((w.B, w.H, w.D), dtype=tdt, device=dev) for _ in range(3))
-    lens_d = torch.empty(w.B, dtype=torch.int32, device=dev)
+    # One pinned staging buffer per step, sent in one copy: the new query, K and V rows
+    # (bf16 [3, B, H, D]), the rows' cache positions (int64 [B], lens - 1, known on the host)
+    # and the lengths (int32 [B]).
+    n_rows = 3 * w.B * w.H * w.D
+    row_bytes, pos_bytes = n_rows * 2, w.B * 8
+    stage_h = torch.empty(row_bytes + pos_bytes + w.B * 4, dtype=torch.uint8).pin_memory()
+    stage_h[:row_bytes].view(tdt).copy_(torch.randn(n_rows, generator=g).to(tdt))
+    lens_cpu = decode_lens()
+    stage_h[row_bytes:row_bytes + pos_bytes].view(torch.int64).copy_(lens_cpu.long() - 1)
+    stage_h[row_bytes + pos_bytes:].view(torch.int32).copy_(lens_cpu)
+    stage_d = torch.empty_like(stage_h, device=dev)
+    rows = stage_d[:row_bytes].view(tdt).view(3, w.B, w.H, w.D)
+    qn, knew, vnew = rows[0], rows[1], rows[2]
+    pos = stage_d[row_bytes:row_bytes + pos_bytes].view(torch.int64)
+    lens_d = stage_d[row_bytes + pos_bytes:].view(torch.int32)
     out_h = torch.empty((w.B, w.H, w.D), dtype=torch.float32).pin_memory()
     bidx = torch.arange(w.B, device=dev)
 
     def one():
-        for h_, d_ in ((q_h, qn), (knew_h, knew), (vnew_h, vnew), (lens_h, lens_d)):
-            d_.copy_(h_, non_blocking=True)
-        pos = (lens_d - 1).long()
+        stage_d.copy_(stage_h, non_blocking=True)
         kc[bidx, :, pos] = knew
         vc[bidx, :, pos] = vnew
         wf.decode(qn, kc, vc, lens_d, out=od, workspace=ws)
@@ -818,9 +826,10 @@ def run_decode(args, ctx: Ctx, w: Workload) -> dict:
     e2e_ms = timed_e2e(ctx, one, steps, args.warmup, False)
     e2e = {"value": kv_bytes * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
            "ms_per_step": e2e_ms, "steps": steps,
-           "h2d_bytes_per_step": 3 * q_h.numel() * q_h.element_size() + lens_h.numel() * 4,
+           "h2d_bytes_per_step": stage_h.numel(),
            "d2h_bytes_per_step": out_h.numel() * 4,
-           "path": "warpforth_b200.warpforth.decode (ctypes) -> libwfattn C ABI; new K/V rows "
+           "path": "warpforth_b200.warpforth.decode (ctypes) -> libwfattn C ABI; the step's "
+                   "new q/K/V rows, cache positions and lengths in one pinned copy, the K/V rows "
                    "scattered into the resident cache"}
     peak = float(ctx.peaks["hbm_gbs"])
     achieved = kv_bytes / (split_ms / 1e3) / 1e9
